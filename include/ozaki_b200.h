@@ -1,0 +1,121 @@
+/*
+ * ozaki_b200.h -- C ABI of the B200 (sm_100a) FP64-on-INT8 (Ozaki-II / CRT) GEMM engine, libozaki_b200.so.
+ *
+ * The engine computes C = A B for float64 A (m x k, row-major) and B (k x n, row-major) from N exact INT8
+ * residue-plane products and a Chinese-Remainder reconstruction, with the moduli set, scaling, plane-count
+ * rule and rounding of the reference engine dl1683/matrix-numbers, code/ozaki_engine.py (citations below are
+ * file:line in that file).  The reference binds its GPU path through ctypes (ozaki_engine.py:20-229); these
+ * entry points replace the calls it makes there, one C function per reference stage.
+ *
+ * Conventions (all entry points):
+ *   - pointers are CUDA device pointers of the current device unless stated otherwise; the caller owns every
+ *     buffer, and no entry point allocates device memory;
+ *   - `stream` is a cudaStream_t (a CUstream handle; NULL = the legacy default stream); work is enqueued, never
+ *     synchronised, so every entry point may be captured in a CUDA graph;
+ *   - the return value is OZK_OK (0) or an error code (ozk_error_string); an error is returned before any
+ *     launch when an argument is invalid;
+ *   - device-side failures (a bounded wait that ran out) are reported through the `err` word of the GEMM
+ *     entry points (bit flags OZK_DEVERR_*), which the caller reads after its next synchronisation.
+ *
+ * Shape rules (the reference's, ozaki_engine.py:1315-1316, except the k bound): m % 4 == 0, n % 32 == 0,
+ * k % 32 == 0, m, n, k > 0.  k has no upper bound here: the products accumulate exactly in segments of 65536
+ * (INT32 cannot overflow inside a segment) and the segments are combined modulo each modulus.
+ */
+#ifndef OZAKI_B200_H
+#define OZAKI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* ozk_stream_t;
+
+#define OZK_OK 0
+#define OZK_ERR_ARG (-1)          /* invalid shape, alignment, null pointer or out-of-range count           */
+#define OZK_ERR_P_RANGE (-2)      /* scaling bits p outside [0, 159]                                        */
+#define OZK_ERR_DEVICE (-3)       /* no CUDA device, or the device is not sm_100                            */
+#define OZK_ERR_DRIVER (-4)       /* driver entry point or TMA tensor-map encoding failed                   */
+#define OZK_ERR_WORKSPACE (-5)    /* workspace smaller than the *_workspace_bytes query                     */
+#define OZK_ERR_CUDA_BASE 1000    /* OZK_ERR_CUDA_BASE + cudaError_t of a failed launch or attribute call  */
+
+#define OZK_DEVERR_TIMEOUT_PRODUCER 1   /* GEMM: the TMA producer's bounded wait ran out   */
+#define OZK_DEVERR_TIMEOUT_MMA 2        /* GEMM: the MMA issuer's bounded wait ran out     */
+#define OZK_DEVERR_TIMEOUT_EPILOGUE 4   /* GEMM: an epilogue warp's bounded wait ran out   */
+
+/* ---- library information -------------------------------------------------------------------------------- */
+int ozk_version(void);
+const char* ozk_error_string(int code);
+/* number of SMs of the current device (the persistent GEMM's grid); OZK_ERR_DEVICE without a device */
+int ozk_device_sm_count(int* out);
+
+/* ---- host helpers (no device work) ----------------------------------------------------------------------- */
+/* modulus t of the fixed list 256, 255, 253, ... 107 (ozaki_engine.py:824-825); 0 outside [0, 32) */
+int ozk_modulus(int t);
+/* float(prod of the first N moduli), correctly rounded (the Mvec of ozaki_engine.py:1160) */
+double ozk_modulus_product(int N);
+/* limb count ceil(bits(prod m)/32), at least 2 (ozaki_engine.py:1104-1106) */
+int ozk_limbs_for(int N);
+/* largest p in [0, 249] with 2 Xmax(p) + 1 <= M_N (ozaki_engine.py:1119-1139) */
+int ozk_pmax_bits(int N, double nuA, double nuB, int k);
+
+/* ---- stage 1: statistics (replaces OzakiCRT.stats, ozaki_engine.py:1229-1247 with kernels :846-951) ------ *
+ * gam[k]: inside scaling gamma_l (0 when inside == 0); r[m], sA[m], nA[m]: row exponent and sums of A;
+ * c[n], sB[n], nB[n]: column exponent (0 for an all-zero column) and sums of B; flag[1]: 1 if a non-finite
+ * value was seen.  Sums are reduced in a fixed order (bitwise reproducible run to run).                    */
+size_t ozk_stats_workspace_bytes(int m, int n, int k);
+int ozk_stats(const double* A, const double* B, int m, int n, int k, int inside, int32_t* gam, int32_t* r,
+              int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag, void* workspace,
+              size_t workspace_bytes, ozk_stream_t stream);
+
+/* ---- stage 2: the a-priori plane-count rule on the device (replaces OzakiCRT.choose, ozaki_engine.py:
+ * 1250-1307, and OzakiCRT._rule_device, :1372-1426).  probe_rows / probe_cols: the random part of the probe
+ * set (RandomState(seed).choice, :1265-1267), device int64; the 32 "hard" rows and columns are added on the
+ * device.  dec[4] = {N (0 on fallback), p, fallback, p_req}; p_dev[1] = p (read by the later stages, so that a
+ * captured graph does not depend on p); aux[8] = {nuA, nuB, worst E/D at p_req, distinct probe rows, distinct
+ * probe columns, 0, 0, 0}.  force_N > 0 skips the probe (N = force_N, p = pmax_bits); force_p >= 0 with
+ * force_N caps p and flags fallback when the data allow less (ozaki_engine.py:1389-1396, :1492-1498).      */
+size_t ozk_rule_workspace_bytes(int m, int n, int k);
+int ozk_rule(const double* A, const double* B, int m, int n, int k, const int32_t* r, const int32_t* c,
+             const double* sA, const double* nA, const double* sB, const double* nB, const int32_t* flag,
+             const int64_t* probe_rows, int n_probe_rows, const int64_t* probe_cols, int n_probe_cols, double tau,
+             double safety, int force_N, int force_p, int32_t* dec, int32_t* p_dev, double* aux, void* workspace,
+             size_t workspace_bytes, ozk_stream_t stream);
+
+/* ---- stage 3a: residue split (replaces resA_k / resB_k, ozaki_engine.py:996-1038 and :1328-1331) --------- *
+ * Ares[t][i][l] = symmetric residue of round(A_il 2^(p - r_i + gam_l)) modulo m_t, t < N, as int8;
+ * Bres[t][j][l] = the same for B_lj 2^(p - c_j - gam_l), contraction index contiguous (K-major planes).     */
+int ozk_split_a(const double* A, const int32_t* r, const int32_t* gam, const int32_t* p_dev, int m, int k, int N,
+                int8_t* Ares, ozk_stream_t stream);
+int ozk_split_b(const double* B, const int32_t* c, const int32_t* gam, const int32_t* p_dev, int k, int n, int N,
+                int8_t* Bres, ozk_stream_t stream);
+
+/* ---- stage 3b: the N INT8 products with the modular reduction fused into the epilogue (replaces the
+ * cuBLASLt INT8 GEMM loop and reduce_k, ozaki_engine.py:1333-1341 and :952-967).  Persistent tcgen05.mma
+ * kind::i8 kernel fed by TMA; the INT32 accumulators live in TMEM and never reach HBM.
+ * X[t][i][j] = (sum_l Ares[t][i][l] Bres[t][j][l]) mod m_t in [0, m_t).  err: device int32, OR'ed flags.   */
+int ozk_gemm_residues(const int8_t* Ares, const int8_t* Bres, int m, int n, int k, int N, uint8_t* X, int32_t* err,
+                      ozk_stream_t stream);
+/* The same kernel with an INT32 epilogue, for one plane pair: C32 = A_plane B_plane^T (the per-modulus
+ * product of ozaki_engine.py:1336, exact while k <= 131071).                                                 */
+int ozk_gemm_i32(const int8_t* A_plane, const int8_t* B_plane, int m, int n, int k, int32_t* C32, int32_t* err,
+                 ozk_stream_t stream);
+
+/* ---- stage 3c: CRT reconstruction and unscale (replaces recon_k, ozaki_engine.py:1040-1101) ------------- *
+ * C[i][j] = the correctly rounded double of the symmetric CRT lift of X[.][i][j], times 2^(r_i + c_j - 2p)
+ * (the ldexp rounding of the reference in the subnormal range).                                            */
+int ozk_reconstruct(const uint8_t* X, const int32_t* r, const int32_t* c, const int32_t* p_dev, int m, int n, int N,
+                    double* C, ozk_stream_t stream);
+
+/* ---- stage 3 in one call (replaces OzakiCRT.core, ozaki_engine.py:1310-1350): split A (unless skip_a),
+ * split B, products, reconstruction.                                                                        */
+int ozk_core(const double* A, const double* B, const int32_t* gam, const int32_t* r, const int32_t* c,
+             const int32_t* p_dev, int m, int n, int k, int N, int skip_a, int8_t* Ares, int8_t* Bres, uint8_t* X,
+             double* C, int32_t* err, ozk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OZAKI_B200_H */

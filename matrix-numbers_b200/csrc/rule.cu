@@ -1,0 +1,389 @@
+// Stage 2: the a-priori plane-count rule (Lemma L1 on a probe set), entirely on the device.
+//
+// Mathematics of the reference's host rule OzakiCRT.choose (code/ozaki_engine.py:1250-1307):
+//   nu_A = sqrt(max nA), nu_B = sqrt(max nB); pv[N] = pmax_bits(N, nu_A, nu_B, k) for N = 6..32 (:1119-1139);
+//   probe rows I = random rows (RandomState(seed), given by the caller) + the 32 largest 2^r_i k / sA_i, columns J
+//   likewise (:1265-1271); D = |A_I| |B_J| (:1277); F1 = (2^r_i sB_j + 2^c_j sA_i) / 2, F2 = k 2^(r_i + c_j) / 4;
+//   p_req = smallest p >= 1 with (F1 2^-p + F2 2^-2p) * safety <= tau * D on every probe entry with D > 0, searched
+//   by the two while-loops of :1290-1296 (capped at 249); N = smallest N in [6, 32] with pv[N] >= p_req, else
+//   fallback (:1300-1307).  The forced-configuration branch follows _rule_device (:1387-1396).
+//
+// The loop conditions are evaluated with explicitly rounded double operations (__dmul_rn, __dadd_rn), one rounding
+// per operation as numpy does, so the decisions equal the host rule's for equal statistics and equal D.  Because
+// ok(p) is monotone in p, the smallest p is found per probe entry and p_req is their maximum.
+//
+// Kernels: rule_prep (1 block: nu, pv, forced / non-finite decisions, the top-32 selections), probe_partial
+// (split-K FP64 probe product), probe_reduce (partials added in block order), rule_final (1 block: p_req, N, p,
+// worst E/D).
+#include <math.h>
+
+#include "ozk_common.cuh"
+
+namespace {
+
+constexpr int kProbeMax = 96;          // at most 64 random + 32 hard indices per side
+constexpr int kPrepThreads = 1024;
+constexpr int kFinalThreads = 1024;
+constexpr int kProbeThreads = 256;
+constexpr int kProbeK = 16;            // contraction rows per smem tile of the probe product
+constexpr double kOnePlus = 1.0 + 1e-9;
+
+struct MTable { double M[OZK_NMAX + 1]; };   // M[N] = float(prod of the first N moduli)
+
+struct RuleCtl {            // lives at the start of the workspace
+    int done;               // 1: the decision is already made (forced N, non-finite input)
+    int nI, nJ;
+    int pad;
+    int pv[OZK_NMAX + 1];
+    double nuA, nuB;
+    int I[kProbeMax];
+    int J[kProbeMax];
+};
+
+__device__ __forceinline__ bool fits(int p, double nuA, double nuB, double sk, double M) {
+    const double tp = ldexp(1.0, p);
+    const double x = __dadd_rn(__dmul_rn(tp, nuA), sk);
+    const double y = __dadd_rn(__dmul_rn(tp, nuB), sk);
+    double v = __dmul_rn(2.0, x);
+    v = __dmul_rn(v, y);
+    v = __dmul_rn(v, kOnePlus);
+    v = __dadd_rn(v, 2.0);
+    return v <= M;
+}
+
+// largest p in [0, 249] with fits(p): closed-form start, then the reference's fix-up loops (:1119-1139)
+__device__ int pmax_bits_dev(double M, double nuA, double nuB, int k) {
+    const double sk = __dmul_rn(__dsqrt_rn((double)k), 0.5);
+    if (!fits(0, nuA, nuB, sk, M)) return 0;
+    const double a = nuA * nuB, bq = sk * (nuA + nuB), cq = sk * sk - (M - 2.0) / (2.0 * kOnePlus);
+    double y;
+    if (a == 0.0) y = bq > 0.0 ? -cq / bq : ldexp(1.0, 249);
+    else y = (-bq + sqrt(fmax(bq * bq - 4.0 * a * cq, 0.0))) / (2.0 * a);
+    int p = 0;
+    if (y > 0.0) { const double f = floor(log2(y)); p = f < 0.0 ? 0 : (f > 249.0 ? 249 : (int)f); }
+    while (p > 0 && !fits(p, nuA, nuB, sk, M)) p--;
+    while (p < 249 && fits(p + 1, nuA, nuB, sk, M)) p++;
+    return p;
+}
+
+__device__ __forceinline__ double hard_value(int e, double s, int k) {
+    // 2^e k / s where s > 0, else 0 (:1269-1270)
+    return s > 0.0 ? __ddiv_rn(__dmul_rn(ldexp(1.0, e), (double)k), s) : 0.0;
+}
+
+// (v, i) precedes (bv, bi) in the order "larger value first, then lower index" (a stable descending sort)
+__device__ __forceinline__ bool before(double v, int i, double bv, int bi) {
+    return v > bv || (v == bv && i < bi);
+}
+
+// Select the `cnt` first indices of the stable descending order of hard values; writes them to out[0..cnt).
+__device__ void top_hard(const int32_t* __restrict__ e, const double* __restrict__ s, int len, int k, int cnt, int* out,
+                         double* smv, int* smi) {
+    double pv = INFINITY;
+    int pi = -1;
+    for (int round = 0; round < cnt; round++) {
+        double bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int x = threadIdx.x; x < len; x += blockDim.x) {
+            const double v = hard_value(e[x], s[x], k);
+            const bool after_prev = (v < pv) || (v == pv && x > pi);
+            if (after_prev && before(v, x, bv, bi)) { bv = v; bi = x; }
+        }
+        // block argmax in the same order
+        for (int o = 16; o > 0; o >>= 1) {
+            const double ov = __shfl_down_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+            if (before(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+        __syncthreads();
+        if (ln == 0) { smv[w] = bv; smi[w] = bi; }
+        __syncthreads();
+        if (w == 0) {
+            bv = ln < (int)(blockDim.x >> 5) ? smv[ln] : -INFINITY;
+            bi = ln < (int)(blockDim.x >> 5) ? smi[ln] : 0x7fffffff;
+            for (int o = 16; o > 0; o >>= 1) {
+                const double ov = __shfl_down_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+                if (before(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+            }
+            if (ln == 0) { smv[0] = bv; smi[0] = bi; }
+        }
+        __syncthreads();
+        pv = smv[0];
+        pi = smi[0];
+        __syncthreads();
+        if (pi == 0x7fffffff) pi = 0;   // only non-comparable (NaN) values left: fall back to index 0
+        if (threadIdx.x == 0) out[round] = pi;
+    }
+}
+
+__device__ double block_max(double v, double* sm) {
+    for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_down_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double a = sm[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) a = fmax(a, sm[w]);
+        sm[0] = a;
+    }
+    __syncthreads();
+    const double r = sm[0];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
+    const int32_t* __restrict__ r, const int32_t* __restrict__ c, const double* __restrict__ sA,
+    const double* __restrict__ nA, const double* __restrict__ sB, const double* __restrict__ nB,
+    const int32_t* __restrict__ flag, const int64_t* __restrict__ Ir, int nIr, const int64_t* __restrict__ Jr, int nJr,
+    int m, int n, int k, int force_N, int force_p, MTable mt, RuleCtl* __restrict__ ctl, int32_t* __restrict__ dec,
+    int32_t* __restrict__ p_dev, double* __restrict__ aux) {
+    __shared__ double smv[32];
+    __shared__ int smi[32];
+    // max nA, max nB (order-independent)
+    double mA = 0.0, mB = 0.0;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) mA = fmax(mA, nA[i]);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) mB = fmax(mB, nB[j]);
+    mA = block_max(mA, smv);
+    mB = block_max(mB, smv);
+    if (threadIdx.x == 0) { ctl->nuA = __dsqrt_rn(mA); ctl->nuB = __dsqrt_rn(mB); }
+    __syncthreads();
+    const double nuA = ctl->nuA, nuB = ctl->nuB;
+    if (threadIdx.x >= 1 && threadIdx.x <= OZK_NMAX) ctl->pv[threadIdx.x] = pmax_bits_dev(mt.M[threadIdx.x], nuA, nuB, k);
+    __syncthreads();
+    const int nonfinite = flag[0] != 0;
+    if (nonfinite || force_N > 0) {
+        if (threadIdx.x == 0) {
+            int N = 0, p = 0, fb = 1;
+            if (!nonfinite) {
+                p = ctl->pv[force_N];
+                fb = 0;
+                if (force_p >= 0) { fb = p < force_p; p = min(p, force_p); }
+                N = fb ? 0 : force_N;
+            }
+            dec[0] = N; dec[1] = p; dec[2] = fb; dec[3] = 0;
+            *p_dev = p;
+            aux[0] = nuA; aux[1] = nuB; aux[2] = 0.0; aux[3] = 0.0; aux[4] = 0.0;
+            aux[5] = 0.0; aux[6] = 0.0; aux[7] = 0.0;
+            ctl->done = 1;
+        }
+        return;
+    }
+    const int hr = min(32, m), hc = min(32, n);
+    if (threadIdx.x == 0) { ctl->done = 0; ctl->nI = nIr + hr; ctl->nJ = nJr + hc; }
+    // caller-supplied probe indices are clamped into range (an out-of-range index must not be dereferenced)
+    for (int x = threadIdx.x; x < nIr; x += blockDim.x) ctl->I[x] = (Ir[x] >= 0 && Ir[x] < m) ? (int)Ir[x] : 0;
+    for (int x = threadIdx.x; x < nJr; x += blockDim.x) ctl->J[x] = (Jr[x] >= 0 && Jr[x] < n) ? (int)Jr[x] : 0;
+    top_hard(r, sA, m, k, hr, ctl->I + nIr, smv, smi);
+    top_hard(c, sB, n, k, hc, ctl->J + nJr, smv, smi);
+}
+
+// split-K probe product: partial[b][a][j] = sum over this block's contraction tiles of |A_I[a] l| |B_l J[j]|
+__global__ void __launch_bounds__(kProbeThreads) probe_partial_kernel(const double* __restrict__ A, const double* __restrict__ B,
+                                                                      int n, int k, const RuleCtl* __restrict__ ctl,
+                                                                      double* __restrict__ partial) {
+    if (ctl->done) return;
+    __shared__ double sa[kProbeMax][kProbeK + 1];
+    __shared__ double sb[kProbeK][kProbeMax];
+    __shared__ int sI[kProbeMax], sJ[kProbeMax];
+    const int nI = ctl->nI, nJ = ctl->nJ;
+    for (int x = threadIdx.x; x < kProbeMax; x += blockDim.x) {
+        sI[x] = x < nI ? ctl->I[x] : -1;
+        sJ[x] = x < nJ ? ctl->J[x] : -1;
+    }
+    const int a0 = (threadIdx.x >> 4) * 6, b0 = (threadIdx.x & 15) * 6;
+    double acc[6][6];
+#pragma unroll
+    for (int u = 0; u < 6; u++)
+#pragma unroll
+        for (int v = 0; v < 6; v++) acc[u][v] = 0.0;
+    const int ntiles = (k + kProbeK - 1) / kProbeK;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int l0 = tile * kProbeK;
+        __syncthreads();
+        for (int x = threadIdx.x; x < kProbeMax * kProbeK; x += blockDim.x) {
+            const int a = x / kProbeK, l = x % kProbeK;
+            const int row = sI[a];
+            sa[a][l] = (row >= 0 && l0 + l < k) ? fabs(__ldg(A + (size_t)row * k + l0 + l)) : 0.0;
+        }
+        for (int x = threadIdx.x; x < kProbeMax * kProbeK; x += blockDim.x) {
+            const int l = x / kProbeMax, b = x % kProbeMax;
+            const int col = sJ[b];
+            sb[l][b] = (col >= 0 && l0 + l < k) ? fabs(__ldg(B + (size_t)(l0 + l) * n + col)) : 0.0;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int l = 0; l < kProbeK; l++) {
+            double av[6], bv[6];
+#pragma unroll
+            for (int u = 0; u < 6; u++) av[u] = sa[a0 + u][l];
+#pragma unroll
+            for (int v = 0; v < 6; v++) bv[v] = sb[l][b0 + v];
+#pragma unroll
+            for (int u = 0; u < 6; u++)
+#pragma unroll
+                for (int v = 0; v < 6; v++) acc[u][v] = fma(av[u], bv[v], acc[u][v]);
+        }
+    }
+    double* out = partial + (size_t)blockIdx.x * kProbeMax * kProbeMax;
+#pragma unroll
+    for (int u = 0; u < 6; u++)
+#pragma unroll
+        for (int v = 0; v < 6; v++) out[(a0 + u) * kProbeMax + b0 + v] = acc[u][v];
+}
+
+// D[a][b] = sum of the per-block partials in block order (fixed order: bitwise reproducible)
+__global__ void probe_reduce_kernel(const double* __restrict__ partial, int nblocks, const RuleCtl* __restrict__ ctl,
+                                    double* __restrict__ D) {
+    if (ctl->done) return;
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= kProbeMax * kProbeMax) return;
+    double s = 0.0;
+    for (int h = 0; h < nblocks; h++) s += partial[(size_t)h * kProbeMax * kProbeMax + e];
+    D[e] = s;
+}
+
+struct EntryTerms { double F1, F2, rhs; };   // rhs = tau * D
+
+__device__ __forceinline__ bool ok_entry(const EntryTerms& t, int p, double safety) {
+    const double E = __dadd_rn(__dmul_rn(t.F1, ldexp(1.0, -p)), __dmul_rn(t.F2, ldexp(1.0, -2 * p)));
+    return __dmul_rn(E, safety) <= t.rhs;
+}
+
+__global__ void __launch_bounds__(kFinalThreads) rule_final_kernel(
+    const int32_t* __restrict__ r, const int32_t* __restrict__ c, const double* __restrict__ sA,
+    const double* __restrict__ sB, int k, double tau, double safety, const double* __restrict__ Dg,
+    RuleCtl* __restrict__ ctl, int32_t* __restrict__ dec, int32_t* __restrict__ p_dev, double* __restrict__ aux) {
+    if (ctl->done) return;
+    __shared__ int s_red[32];
+    __shared__ double s_redd[32];
+    __shared__ int s_preq;
+    const int nI = ctl->nI, nJ = ctl->nJ;
+    const int cnt = nI * nJ;
+    const double k4 = 0.25 * (double)k;
+    // pass 1: smallest p per entry, maximum over entries
+    int mx = 1;
+    for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
+        const int a = e / nJ, b = e % nJ;
+        const double D = Dg[a * kProbeMax + b];
+        if (!(D > 0.0)) continue;
+        const int i = ctl->I[a], j = ctl->J[b];
+        EntryTerms t;
+        const int ri = r[i], cj = c[j];
+        t.F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(ldexp(1.0, ri), sB[j]), __dmul_rn(ldexp(1.0, cj), sA[i])));
+        t.F2 = __dmul_rn(k4, ldexp(1.0, ri + cj));
+        t.rhs = __dmul_rn(tau, D);
+        // closed-form start (largest 2^-p meeting E <= tau D / safety), then exact fix-up
+        const double cq = tau * D / safety;
+        const double xm = 2.0 * cq / (t.F1 + sqrt(t.F1 * t.F1 + 4.0 * t.F2 * cq));
+        const double est = ceil(-log2(xm));
+        int p = est != est ? 250 : (est < 1.0 ? 1 : (est > 250.0 ? 250 : (int)est));
+        while (p > 1 && ok_entry(t, p - 1, safety)) p--;
+        while (p < 250 && !ok_entry(t, p, safety)) p++;
+        mx = max(mx, p);
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_down_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int v = 1;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) v = max(v, s_red[w]);
+        s_preq = v;
+    }
+    __syncthreads();
+    const int preq = min(s_preq, 249);
+    // pass 2: worst E / D at p_req (the host rule's info, :1297-1298)
+    double worst = 0.0;
+    for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
+        const int a = e / nJ, b = e % nJ;
+        const double D = Dg[a * kProbeMax + b];
+        if (!(D > 0.0)) continue;
+        const int i = ctl->I[a], j = ctl->J[b];
+        const int ri = r[i], cj = c[j];
+        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(ldexp(1.0, ri), sB[j]), __dmul_rn(ldexp(1.0, cj), sA[i])));
+        const double F2 = __dmul_rn(k4, ldexp(1.0, ri + cj));
+        const double E = __dadd_rn(__dmul_rn(F1, ldexp(1.0, -preq)), __dmul_rn(F2, ldexp(1.0, -2 * preq)));
+        worst = fmax(worst, __ddiv_rn(E, D));
+    }
+    for (int o = 16; o > 0; o >>= 1) worst = fmax(worst, __shfl_down_sync(0xffffffffu, worst, o));
+    if ((threadIdx.x & 31) == 0) s_redd[threadIdx.x >> 5] = worst;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double w = 0.0;
+        for (int q = 0; q < (int)(blockDim.x >> 5); q++) w = fmax(w, s_redd[q]);
+        int N = 0, p = 0;
+        const bool over = s_preq > 249;
+        if (!over) {
+            for (int q = 6; q <= OZK_NMAX; q++)
+                if (ctl->pv[q] >= preq) { N = q; p = ctl->pv[q]; break; }
+        }
+        const int fb = N == 0;
+        dec[0] = N; dec[1] = p; dec[2] = fb; dec[3] = preq;
+        *p_dev = p;
+        int du = 0, dv = 0;
+        for (int a = 0; a < nI; a++) {
+            bool seen = false;
+            for (int b = 0; b < a; b++) seen |= ctl->I[b] == ctl->I[a];
+            du += !seen;
+        }
+        for (int a = 0; a < nJ; a++) {
+            bool seen = false;
+            for (int b = 0; b < a; b++) seen |= ctl->J[b] == ctl->J[a];
+            dv += !seen;
+        }
+        aux[0] = ctl->nuA; aux[1] = ctl->nuB; aux[2] = w; aux[3] = (double)du; aux[4] = (double)dv;
+        aux[5] = 0.0; aux[6] = 0.0; aux[7] = 0.0;
+    }
+}
+
+int probe_blocks(int k) {
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = (k + kProbeK - 1) / kProbeK;
+    return max(1, min(tiles, 2 * sms));
+}
+
+}  // namespace
+
+extern "C" size_t ozk_rule_workspace_bytes(int m, int n, int k) {
+    if (m <= 0 || n <= 0 || k <= 0) return 0;
+    const size_t ctl = (sizeof(RuleCtl) + 255) & ~(size_t)255;
+    return ctl + (size_t)(probe_blocks(k) + 1) * kProbeMax * kProbeMax * sizeof(double);
+}
+
+extern "C" int ozk_rule(const double* A, const double* B, int m, int n, int k, const int32_t* r, const int32_t* c,
+                        const double* sA, const double* nA, const double* sB, const double* nB, const int32_t* flag,
+                        const int64_t* probe_rows, int n_probe_rows, const int64_t* probe_cols, int n_probe_cols,
+                        double tau, double safety, int force_N, int force_p, int32_t* dec, int32_t* p_dev, double* aux,
+                        void* workspace, size_t workspace_bytes, ozk_stream_t stream_) {
+    if (!A || !B || !r || !c || !sA || !nA || !sB || !nB || !flag || !dec || !p_dev || !aux || !workspace)
+        return OZK_ERR_ARG;
+    if (m <= 0 || n <= 0 || k <= 0) return OZK_ERR_ARG;
+    if (force_N != 0 && (force_N < 1 || force_N > OZK_NMAX)) return OZK_ERR_ARG;
+    if (force_N == 0) {
+        if (n_probe_rows < 0 || n_probe_rows > 64 || n_probe_cols < 0 || n_probe_cols > 64) return OZK_ERR_ARG;
+        if ((n_probe_rows && !probe_rows) || (n_probe_cols && !probe_cols)) return OZK_ERR_ARG;
+    }
+    if (workspace_bytes < ozk_rule_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    MTable mt;
+    for (int N = 0; N <= OZK_NMAX; N++) mt.M[N] = N ? ozk_modulus_product(N) : 1.0;
+    RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
+    double* partial = reinterpret_cast<double*>(static_cast<char*>(workspace) + ((sizeof(RuleCtl) + 255) & ~(size_t)255));
+    const int nb = probe_blocks(k);
+    rule_prep_kernel<<<1, kPrepThreads, 0, st>>>(r, c, sA, nA, sB, nB, flag, probe_rows, n_probe_rows, probe_cols,
+                                                 n_probe_cols, m, n, k, force_N, force_N > 0 ? force_p : -1, mt, ctl, dec,
+                                                 p_dev, aux);
+    OZK_CHECK_LAUNCH();
+    probe_partial_kernel<<<nb, kProbeThreads, 0, st>>>(A, B, n, k, ctl, partial);
+    OZK_CHECK_LAUNCH();
+    double* D = partial + (size_t)nb * kProbeMax * kProbeMax;
+    probe_reduce_kernel<<<(kProbeMax * kProbeMax + 255) / 256, 256, 0, st>>>(partial, nb, ctl, D);
+    OZK_CHECK_LAUNCH();
+    rule_final_kernel<<<1, kFinalThreads, 0, st>>>(r, c, sA, sB, k, tau, safety, D, ctl, dec, p_dev, aux);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}

@@ -1,0 +1,234 @@
+// Stage 1: per-index statistics of A and B (the reference's CU_STATS kernels, code/ozaki_engine.py:846-951,
+// launched in the order of OzakiCRT.stats, :1229-1247).
+//
+// Differences from the reference, by design:
+//   - every sum is reduced in a fixed order (per-thread strided sums, a fixed shuffle tree, then partial sums per
+//     row chunk added in chunk order), so sB / nB are bitwise reproducible; the reference adds them with double
+//     atomicAdd (:949-950), whose order varies from run to run;
+//   - loads are 16-byte vectors, coalesced along the contiguous index of each matrix.
+#include "ozk_common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kColmaxRows = 64;     // rows of A folded by one block of colmax_a_kernel
+constexpr int kColChunk = 512;      // rows of B folded by one block of the column kernels
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, T identity, T* sm, Op op) {
+    // fixed-order tree: warp shuffle, then warp 0 over the per-warp results; the result is broadcast
+    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_down_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    __syncthreads();
+    if (ln == 0) sm[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        v = ln < (int)(blockDim.x >> 5) ? sm[ln] : identity;
+        for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_down_sync(0xffffffffu, v, o));
+        if (ln == 0) sm[0] = v;
+    }
+    __syncthreads();
+    T r = sm[0];
+    __syncthreads();
+    return r;
+}
+
+__device__ __forceinline__ double block_sum(double v, double* sm) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    __syncthreads();
+    if (ln == 0) sm[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        v = ln < (int)(blockDim.x >> 5) ? sm[ln] : 0.0;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+        if (ln == 0) sm[0] = v;
+    }
+    __syncthreads();
+    double r = sm[0];
+    __syncthreads();
+    return r;
+}
+
+struct MaxU64 { __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a > b ? a : b; } };
+struct MaxI { __device__ int operator()(int a, int b) const { return a > b ? a : b; } };
+
+// column max of |A| bit patterns (colmax_k, :847-854): 2 columns per thread, kColmaxRows rows per block
+__global__ void __launch_bounds__(kThreads) colmax_a_kernel(const double* __restrict__ A, unsigned long long* __restrict__ colmax,
+                                                            int m, int k) {
+    const int l = 2 * (blockIdx.x * kThreads + threadIdx.x);
+    if (l >= k) return;
+    const int i0 = blockIdx.y * kColmaxRows, i1 = min(m, i0 + kColmaxRows);
+    unsigned long long m0 = 0, m1 = 0;
+    for (int i = i0; i < i1; i++) {
+        const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2*>(A + (size_t)i * k + l));
+        m0 = max(m0, v.x & OZK_ABSMASK);
+        m1 = max(m1, v.y & OZK_ABSMASK);
+    }
+    atomicMax(colmax + l, m0);
+    atomicMax(colmax + l + 1, m1);
+}
+
+// row max of |B| bit patterns (rowmax_k, :855-869): one block per row of B
+__global__ void __launch_bounds__(kThreads) rowmax_b_kernel(const double* __restrict__ B, unsigned long long* __restrict__ rowmax, int n) {
+    __shared__ unsigned long long sm[32];
+    const int l = blockIdx.x;
+    const ulonglong2* row = reinterpret_cast<const ulonglong2*>(B + (size_t)l * n);
+    unsigned long long mx = 0;
+    for (int j = threadIdx.x; j < n / 2; j += kThreads) {
+        const ulonglong2 v = __ldg(row + j);
+        mx = max(mx, max(v.x & OZK_ABSMASK, v.y & OZK_ABSMASK));
+    }
+    mx = block_reduce(mx, 0ULL, sm, MaxU64());
+    if (threadIdx.x == 0) rowmax[l] = mx;
+}
+
+// gamma_l = (e_B - e_A) >> 1, 0 when disabled, when either side is zero or non-finite (gamma_k, :870-879)
+__global__ void gamma_kernel(const unsigned long long* __restrict__ colmax, const unsigned long long* __restrict__ rowmax,
+                             int32_t* __restrict__ gam, int32_t* __restrict__ flag, int k, int enable) {
+    const int l = blockIdx.x * blockDim.x + threadIdx.x;
+    if (l >= k) return;
+    const unsigned long long a = colmax[l], b = rowmax[l];
+    const bool bad = ((a >> 52) == 0x7ffULL) || ((b >> 52) == 0x7ffULL);
+    if (bad) atomicOr(flag, 1);
+    const int ea = ozk_fexp(a), eb = ozk_fexp(b);
+    gam[l] = (!enable || bad || ea == OZK_NEG || eb == OZK_NEG) ? 0 : ((eb - ea) >> 1);
+}
+
+// r_i = max_l (e(A_il) + gamma_l) over non-zeros (0 if none); sA_i = sum |A_il| 2^gamma_l;
+// nA_i = sum (|A_il| 2^(gamma_l - r_i))^2   (rowstatsA_k, :904-925); one block per row
+__global__ void __launch_bounds__(kThreads) rowstats_a_kernel(const double* __restrict__ A, const int32_t* __restrict__ gam, int k,
+                                                              int32_t* __restrict__ r_out, double* __restrict__ s_out,
+                                                              double* __restrict__ n_out) {
+    __shared__ int smi[32];
+    __shared__ double smd[32];
+    const int i = blockIdx.x;
+    const double2* row = reinterpret_cast<const double2*>(A + (size_t)i * k);
+    const int2* g2 = reinterpret_cast<const int2*>(gam);
+    int mx = OZK_NEG;
+    for (int h = threadIdx.x; h < k / 2; h += kThreads) {
+        const double2 v = __ldg(row + h);
+        const int2 g = __ldg(g2 + h);
+        int e0 = ozk_fexp(ozk_bits(v.x) & OZK_ABSMASK), e1 = ozk_fexp(ozk_bits(v.y) & OZK_ABSMASK);
+        if (e0 != OZK_NEG) mx = max(mx, e0 + g.x);
+        if (e1 != OZK_NEG) mx = max(mx, e1 + g.y);
+    }
+    int rr = block_reduce(mx, (int)OZK_NEG, smi, MaxI());
+    if (rr <= OZK_NEG / 2) rr = 0;
+    double s = 0.0, q = 0.0;
+    for (int h = threadIdx.x; h < k / 2; h += kThreads) {
+        const double2 v = __ldg(row + h);
+        const int2 g = __ldg(g2 + h);
+        const double x0 = fabs(v.x), x1 = fabs(v.y);
+        if (x0 != 0.0) { s += ldexp(x0, g.x); const double y = ldexp(x0, g.x - rr); q += y * y; }
+        if (x1 != 0.0) { s += ldexp(x1, g.y); const double y = ldexp(x1, g.y - rr); q += y * y; }
+    }
+    s = block_sum(s, smd);
+    q = block_sum(q, smd);
+    if (threadIdx.x == 0) { r_out[i] = rr; s_out[i] = s; n_out[i] = q; }
+}
+
+__global__ void fill_i32_kernel(int32_t* __restrict__ p, int count, int v) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) p[i] = v;
+}
+
+// c_j = max_l (e(B_lj) - gamma_l) over non-zeros (colexpB_k, :926-937): 2 columns per thread, kColChunk rows
+__global__ void __launch_bounds__(kThreads) colexp_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ gam, int k,
+                                                            int n, int32_t* __restrict__ c_out) {
+    const int j = 2 * (blockIdx.x * kThreads + threadIdx.x);
+    if (j >= n) return;
+    const int l0 = blockIdx.y * kColChunk, l1 = min(k, l0 + kColChunk);
+    int m0 = OZK_NEG, m1 = OZK_NEG;
+    for (int l = l0; l < l1; l++) {
+        const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2*>(B + (size_t)l * n + j));
+        const int g = __ldg(gam + l);
+        const int e0 = ozk_fexp(v.x & OZK_ABSMASK), e1 = ozk_fexp(v.y & OZK_ABSMASK);
+        if (e0 != OZK_NEG) m0 = max(m0, e0 - g);
+        if (e1 != OZK_NEG) m1 = max(m1, e1 - g);
+    }
+    if (m0 > OZK_NEG / 2) atomicMax(c_out + j, m0);
+    if (m1 > OZK_NEG / 2) atomicMax(c_out + j + 1, m1);
+}
+
+// partial sB / nB over one chunk of rows (colsumsB_k, :938-951), written per chunk instead of atomically added
+__global__ void __launch_bounds__(kThreads) colsums_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ gam,
+                                                             const int32_t* __restrict__ c, int k, int n,
+                                                             double* __restrict__ ps, double* __restrict__ pq) {
+    const int j = 2 * (blockIdx.x * kThreads + threadIdx.x);
+    if (j >= n) return;
+    int c0 = c[j], c1 = c[j + 1];
+    if (c0 <= OZK_NEG / 2) c0 = 0;
+    if (c1 <= OZK_NEG / 2) c1 = 0;
+    const int l0 = blockIdx.y * kColChunk, l1 = min(k, l0 + kColChunk);
+    double s0 = 0.0, s1 = 0.0, q0 = 0.0, q1 = 0.0;
+    for (int l = l0; l < l1; l++) {
+        const double2 v = __ldg(reinterpret_cast<const double2*>(B + (size_t)l * n + j));
+        const int g = __ldg(gam + l);
+        const double x0 = fabs(v.x), x1 = fabs(v.y);
+        if (x0 != 0.0) { s0 += ldexp(x0, -g); const double y = ldexp(x0, -g - c0); q0 += y * y; }
+        if (x1 != 0.0) { s1 += ldexp(x1, -g); const double y = ldexp(x1, -g - c1); q1 += y * y; }
+    }
+    const size_t o = (size_t)blockIdx.y * n + j;
+    ps[o] = s0; ps[o + 1] = s1;
+    pq[o] = q0; pq[o + 1] = q1;
+}
+
+// chunk partials summed in chunk order; c normalised (no non-zero -> 0, as its consumers do at :1257, :1060)
+__global__ void colsums_final_kernel(const double* __restrict__ ps, const double* __restrict__ pq, int nchunks, int n,
+                                     int32_t* __restrict__ c, double* __restrict__ sB, double* __restrict__ nB) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    double s = 0.0, q = 0.0;
+    for (int h = 0; h < nchunks; h++) { s += ps[(size_t)h * n + j]; q += pq[(size_t)h * n + j]; }
+    sB[j] = s;
+    nB[j] = q;
+    if (c[j] <= OZK_NEG / 2) c[j] = 0;
+}
+
+}  // namespace
+
+static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+extern "C" size_t ozk_stats_workspace_bytes(int m, int n, int k) {
+    if (m <= 0 || n <= 0 || k <= 0) return 0;
+    const size_t nchunks = ((size_t)k + kColChunk - 1) / kColChunk;
+    return align256((size_t)k * 8) * 2 + align256(nchunks * (size_t)n * 8) * 2;
+}
+
+extern "C" int ozk_stats(const double* A, const double* B, int m, int n, int k, int inside, int32_t* gam, int32_t* r,
+                         int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag, void* workspace,
+                         size_t workspace_bytes, ozk_stream_t stream_) {
+    if (!A || !B || !gam || !r || !c || !sA || !nA || !sB || !nB || !flag || !workspace) return OZK_ERR_ARG;
+    if (m <= 0 || n <= 0 || k <= 0 || (k & 1) || (n & 1)) return OZK_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return OZK_ERR_ARG;
+    if (workspace_bytes < ozk_stats_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    const int nchunks = (k + kColChunk - 1) / kColChunk;
+    char* ws = static_cast<char*>(workspace);
+    unsigned long long* colmax = reinterpret_cast<unsigned long long*>(ws);
+    unsigned long long* rowmax = reinterpret_cast<unsigned long long*>(ws + align256((size_t)k * 8));
+    double* ps = reinterpret_cast<double*>(ws + 2 * align256((size_t)k * 8));
+    double* pq = reinterpret_cast<double*>(ws + 2 * align256((size_t)k * 8) + align256((size_t)nchunks * n * 8));
+
+    if (cudaMemsetAsync(colmax, 0, (size_t)k * 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
+    if (cudaMemsetAsync(flag, 0, 4, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
+    colmax_a_kernel<<<dim3((k / 2 + kThreads - 1) / kThreads, (m + kColmaxRows - 1) / kColmaxRows), kThreads, 0, st>>>(A, colmax, m, k);
+    OZK_CHECK_LAUNCH();
+    rowmax_b_kernel<<<k, kThreads, 0, st>>>(B, rowmax, n);
+    OZK_CHECK_LAUNCH();
+    gamma_kernel<<<(k + 255) / 256, 256, 0, st>>>(colmax, rowmax, gam, flag, k, inside ? 1 : 0);
+    OZK_CHECK_LAUNCH();
+    rowstats_a_kernel<<<m, kThreads, 0, st>>>(A, gam, k, r, sA, nA);
+    OZK_CHECK_LAUNCH();
+    fill_i32_kernel<<<(n + 255) / 256, 256, 0, st>>>(c, n, OZK_NEG);
+    OZK_CHECK_LAUNCH();
+    const dim3 g2((n / 2 + kThreads - 1) / kThreads, nchunks);
+    colexp_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, c);
+    OZK_CHECK_LAUNCH();
+    colsums_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, c, k, n, ps, pq);
+    OZK_CHECK_LAUNCH();
+    colsums_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(ps, pq, nchunks, n, c, sB, nB);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}

@@ -1,0 +1,334 @@
+"""``OzakiCRT``: drop-in replacement of the reference engine's Python entry point on B200.
+
+Same constructor, methods, arguments, return values and error conventions as ``OzakiCRT`` in
+dl1683/matrix-numbers code/ozaki_engine.py (:1150-1505); every stage runs in libozaki_b200.so (sm_100a kernels,
+include/ozaki_b200.h), torch provides the device buffers, the stream and the CUDA graphs.
+
+    E = OzakiCRT()
+    C, info = E.run(A, B)                 # eager: stats -> device rule -> one host read -> core
+    C, info = E.run(A, B, C, graph=True)  # timed path: [graph: stats + rule] -> host read of (N, p) -> [graph: core]
+
+A, B: float64 CUDA tensors, row-major, A (m, k), B (k, n), with m % 4 == 0, n % 32 == 0, k % 32 == 0 (the
+reference's shape rule, :1315; its k <= 131071 limit does not apply here: the products are accumulated exactly in
+segments of 65536).  Non-finite input, N > 32 or an unsafe forced p fall back to native FP64 (torch.matmul, cuBLAS
+DGEMM) with ``info["fallback"] = True``, as the reference does.
+
+Differences from the reference: the rule of the eager path runs on the device too (the reference's ``choose`` runs it
+on the host in numpy; both apply the same mathematics, see csrc/rule.cu); every kernel is compiled ahead of time
+(``kernels(N)`` compiles nothing); statistics are reduced in a fixed order (the reference's column sums use double
+atomics).
+"""
+from __future__ import annotations
+
+import time
+
+import numpy as np
+import torch
+
+from . import _lib
+from .constants import MODS, NEG, NMAX, limbs_for, modulus_product, pmax_bits
+from ._lib import check, ptr
+
+DEV = "cuda"
+
+
+def _stream_handle(stream=None) -> int:
+    """cudaStream_t handle of a torch stream (default: the current stream), or an int handle passed through."""
+    s = torch.cuda.current_stream() if stream is None else stream
+    return s.cuda_stream if hasattr(s, "cuda_stream") else int(s)
+
+
+class OzakiCRT:
+    """FP64 GEMM from INT8 residue-plane products and CRT reconstruction (Ozaki scheme II) on B200."""
+
+    def __init__(self, lt=None):
+        # `lt` (the reference's cuBLASLt wrapper) is accepted for signature compatibility and unused: the INT8
+        # products are this library's own tcgen05 kernel.
+        self.lib = _lib.lib()
+        if not torch.cuda.is_available():
+            raise _lib.OzkError("OzakiCRT needs a CUDA device (B200, sm_100a); there is no CPU path")
+        major, _ = torch.cuda.get_device_capability()
+        if major != 10:
+            raise _lib.OzkError(f"OzakiCRT is built for sm_100a (B200); the current device has compute capability {major}.x")
+        self.per_n = {}
+        self.bufs = {}
+        self.graphs = {}
+        self.probe = {}
+        self.Mvec = torch.tensor([modulus_product(N) for N in range(6, NMAX + 1)], dtype=torch.float64, device=DEV)
+        self.launches = 0   # kernels launched by this engine (for the benchmark's launch count)
+
+    # ---- kernels: compiled ahead of time, the per-N tables live in the library ---------------------------------
+    def kernels(self, N):
+        d = self.per_n.get(N)
+        if d is None:
+            d = {"N": N, "L": limbs_for(N)}
+            self.per_n[N] = d
+        return d
+
+    # ---- buffers (engine-owned scratch, grown on demand; growing clears the captured graphs) -------------------
+    def buffers(self, m, n, k, N):
+        key = (m, n, k)
+        b = self.bufs.get(key)
+        if b is None or b["N"] < N:
+            self.bufs.pop(key, None)
+            self.graphs.clear()
+            b = None
+            torch.cuda.empty_cache()
+            cap = max(N, 20)
+            bi = torch.empty(m + n + 1, dtype=torch.int32, device=DEV)          # r | c | flag
+            bd = torch.empty(2 * m + 2 * n, dtype=torch.float64, device=DEV)    # sA | nA | sB | nB
+            ctl = torch.zeros(8, dtype=torch.int32, device=DEV)                 # N, p, fallback, p_req | err | p
+            b = {"N": cap,
+                 "Ares": torch.empty(cap * m * k, dtype=torch.int8, device=DEV),
+                 "Bres": torch.empty(cap * n * k, dtype=torch.int8, device=DEV),
+                 "X": torch.empty(cap * m * n, dtype=torch.uint8, device=DEV),
+                 "gam": torch.empty(k, dtype=torch.int32, device=DEV),
+                 "bi": bi, "bd": bd, "r": bi[:m], "c": bi[m:m + n], "flag": bi[m + n:],
+                 "sA": bd[:m], "nA": bd[m:2 * m], "sB": bd[2 * m:2 * m + n], "nB": bd[2 * m + n:],
+                 "ctl": ctl, "dec": ctl[0:4], "err": ctl[4:5], "pdev": ctl[5:6],
+                 "aux": torch.zeros(8, dtype=torch.float64, device=DEV),
+                 "ws_stats": torch.empty(max(1, self.lib.ozk_stats_workspace_bytes(m, n, k)), dtype=torch.uint8, device=DEV),
+                 "ws_rule": torch.empty(max(1, self.lib.ozk_rule_workspace_bytes(m, n, k)), dtype=torch.uint8, device=DEV),
+                 "hi": torch.empty(m + n + 1, dtype=torch.int32).pin_memory(),
+                 "hd": torch.empty(2 * m + 2 * n, dtype=torch.float64).pin_memory(),
+                 "hctl": torch.zeros(8, dtype=torch.int32).pin_memory(),
+                 "haux": torch.zeros(8, dtype=torch.float64).pin_memory()}
+            self.bufs[key] = b
+        return b
+
+    @staticmethod
+    def _shape_check(A, B, C=None):
+        assert A.dtype == torch.float64 and B.dtype == torch.float64, "A and B must be float64"
+        assert A.is_cuda and B.is_cuda and A.is_contiguous() and B.is_contiguous(), "A and B must be contiguous CUDA tensors"
+        m, k = A.shape
+        k2, n = B.shape
+        assert k == k2, "inner dimensions differ"
+        assert k % 32 == 0 and n % 32 == 0 and m % 4 == 0, "shape rule: k % 32 == 0, n % 32 == 0, m % 4 == 0"
+        if C is not None:
+            assert C.dtype == torch.float64 and C.is_contiguous() and tuple(C.shape) == (m, n), "C must be (m, n) float64"
+
+    def _probe_sets(self, m, n, seed):
+        """Random part of the probe set: RandomState(seed).choice without replacement, rows then columns
+        (ozaki_engine.py:1265-1267, :1397-1403); cached per shape and seed."""
+        key = ("probe", m, n, seed)
+        if key not in self.probe:
+            rs = np.random.RandomState(seed)
+            Ir = rs.choice(m, min(64, m), replace=False)
+            Jr = rs.choice(n, min(64, n), replace=False)
+            self.probe[key] = (torch.as_tensor(Ir, dtype=torch.int64, device=DEV),
+                               torch.as_tensor(Jr, dtype=torch.int64, device=DEV))
+        return self.probe[key]
+
+    # ---- stage 1: statistics ---------------------------------------------------------------------------------
+    def stats(self, A, B, b, inside=True, stream=None):
+        m, k = A.shape
+        n = B.shape[1]
+        st = _stream_handle(stream)
+        rc = self.lib.ozk_stats(ptr(A), ptr(B), m, n, k, 1 if inside else 0, ptr(b["gam"]), ptr(b["r"]), ptr(b["c"]),
+                                ptr(b["sA"]), ptr(b["nA"]), ptr(b["sB"]), ptr(b["nB"]), ptr(b["flag"]),
+                                ptr(b["ws_stats"]), b["ws_stats"].numel(), st)
+        check(rc, "ozk_stats")
+        self.launches += 8
+
+    # ---- stage 2: the a-priori rule on the device ---------------------------------------------------------------
+    def _rule_device(self, A, B, b, tau, safety, force_N=None, force_p=None, seed=0, stream=None):
+        m, k = A.shape
+        n = B.shape[1]
+        Ir, Jr = self._probe_sets(m, n, seed)
+        rc = self.lib.ozk_rule(ptr(A), ptr(B), m, n, k, ptr(b["r"]), ptr(b["c"]), ptr(b["sA"]), ptr(b["nA"]),
+                               ptr(b["sB"]), ptr(b["nB"]), ptr(b["flag"]), ptr(Ir), Ir.numel(), ptr(Jr), Jr.numel(),
+                               float(tau), float(safety), int(force_N or 0),
+                               -1 if force_p is None else int(force_p), ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]),
+                               ptr(b["ws_rule"]), b["ws_rule"].numel(), _stream_handle(stream))
+        check(rc, "ozk_rule")
+        self.launches += 4
+
+    def _stats_rule(self, A, B, b, tau, safety, inside, force_N=None, force_p=None):
+        self.stats(A, B, b, inside)
+        self._rule_device(A, B, b, tau, safety, force_N, force_p, seed=0)
+
+    def _read_ctl(self, b):
+        b["hctl"].copy_(b["ctl"], non_blocking=True)
+        b["haux"].copy_(b["aux"], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        ctl = [int(x) for x in b["hctl"].tolist()]
+        if ctl[4]:
+            raise _lib.OzkError(f"device error flag {ctl[4]:#x} raised by an earlier INT8 GEMM launch "
+                                "(a bounded wait ran out); results of that call are invalid")
+        return ctl, b["haux"].tolist()
+
+    def check_errors(self):
+        """Raise if any GEMM launch of this engine reported a device-side error (reads the flags; synchronises)."""
+        for b in self.bufs.values():
+            self._read_ctl(b)
+
+    def host_stats(self, b, m, n):
+        b["hi"].copy_(b["bi"], non_blocking=True)
+        b["hd"].copy_(b["bd"], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        hi, hd = b["hi"].numpy(), b["hd"].numpy()
+        return {"r": hi[:m].copy(), "c": hi[m:m + n].copy(), "sA": hd[:m].copy(), "nA": hd[m:2 * m].copy(),
+                "sB": hd[2 * m:2 * m + n].copy(), "nB": hd[2 * m + n:].copy()}, bool(hi[m + n] != 0)
+
+    def choose(self, A, B, b, tau=2.0 ** -52, force_N=None, seed=0, safety=2.0, prof=None):
+        """The a-priori rule (ozaki_engine.py:1250-1307), evaluated on the device; returns (N, p, info, host stats)
+        like the reference.  The statistics must have been computed (``stats``)."""
+        m, k = A.shape
+        n = B.shape[1]
+        t0 = time.perf_counter()
+        self._rule_device(A, B, b, tau, safety, force_N, None, seed=seed)
+        ctl, aux = self._read_ctl(b)
+        h, nonfinite = self.host_stats(b, m, n)
+        info = {"nonfinite": nonfinite}
+        if nonfinite:
+            info["fallback"] = True
+            return None, None, info, h
+        info["nuA"], info["nuB"] = aux[0], aux[1]
+        N, p, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
+        if force_N is not None:
+            return int(force_N), p, info, h
+        info["probe"] = [int(aux[3]), int(aux[4])]
+        info["worst_ratio_E_over_D"] = aux[2]
+        info["p_req"] = preq
+        if prof is not None:
+            prof["rule_host"] = time.perf_counter() - t0
+        if fb or N == 0:
+            info["fallback"] = True
+            return None, None, info, h
+        return N, p, info, h
+
+    # ---- stage 3: residues, INT8 products with the fused reduction, reconstruction ------------------------------
+    def core(self, A, B, b, N, C, stream=None, prof=None, skipA=False):
+        m, k = A.shape
+        n = B.shape[1]
+        assert k % 4 == 0 and n % 32 == 0 and m % 4 == 0 and (m * n) % 4 == 0 and k % 32 == 0
+        assert 1 <= N <= NMAX and b["N"] >= N
+        st = _stream_handle(stream)
+        evs = []
+
+        def mark(name):
+            if prof is not None:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                evs.append((name, e))
+        mark("start")
+        if not skipA:
+            check(self.lib.ozk_split_a(ptr(A), ptr(b["r"]), ptr(b["gam"]), ptr(b["pdev"]), m, k, N, ptr(b["Ares"]), st),
+                  "ozk_split_a")
+        check(self.lib.ozk_split_b(ptr(B), ptr(b["c"]), ptr(b["gam"]), ptr(b["pdev"]), k, n, N, ptr(b["Bres"]), st),
+              "ozk_split_b")
+        mark("residues")
+        check(self.lib.ozk_gemm_residues(ptr(b["Ares"]), ptr(b["Bres"]), m, n, k, N, ptr(b["X"]), ptr(b["err"]), st),
+              "ozk_gemm_residues")
+        mark("gemm+reduce")
+        check(self.lib.ozk_reconstruct(ptr(b["X"]), ptr(b["r"]), ptr(b["c"]), ptr(b["pdev"]), m, n, N, ptr(C), st),
+              "ozk_reconstruct")
+        mark("recon")
+        self.launches += 3 if skipA else 4
+        if prof is not None:
+            torch.cuda.synchronize()
+            for (n0, e0), (n1, e1) in zip(evs[:-1], evs[1:]):
+                prof[n1] = prof.get(n1, 0.0) + e0.elapsed_time(e1) / 1e3
+        return C
+
+    def _capture(self, fn):
+        """Eager warm-up on a side stream, then capture on that stream; returns the CUDAGraph."""
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            fn()
+        return g
+
+    def core_graph(self, A, B, b, N, C):
+        key = ("core", A.shape[0], B.shape[1], A.shape[1], N, A.data_ptr(), B.data_ptr(), C.data_ptr())
+        g = self.graphs.get(key)
+        if g is None:
+            g = self._capture(lambda: self.core(A, B, b, N, C))
+            self.graphs[key] = g
+        g.replay()
+        self.launches += 4
+
+    def run_fast(self, A, B, C, tau=2.0 ** -52, safety=2.0, inside=True, force_N=None, force_p=None):
+        """Timed path: [graph: statistics + rule] -> one host read of (N, p) -> [graph: residues, products, recon]."""
+        self._shape_check(A, B, C)
+        m, k = A.shape
+        n = B.shape[1]
+        b = self.buffers(m, n, k, 20)
+        key = ("sr", m, n, k, A.data_ptr(), B.data_ptr(), tau, safety, inside, force_N, force_p)
+        g = self.graphs.get(key)
+        if g is None:
+            g = self._capture(lambda: self._stats_rule(A, B, b, tau, safety, inside, force_N, force_p))
+            self.graphs[key] = g
+        g.replay()
+        self.launches += 12
+        ctl, _ = self._read_ctl(b)
+        N, p, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
+        if fb or N == 0:
+            torch.matmul(A, B, out=C)
+            return C, {"fallback": True, "preq": preq}
+        if b["N"] < N:
+            b = self.buffers(m, n, k, N)
+            g = self._capture(lambda: self._stats_rule(A, B, b, tau, safety, inside, force_N, force_p))
+            self.graphs[key] = g
+            g.replay()
+            ctl, _ = self._read_ctl(b)
+            N, p = ctl[0], ctl[1]
+        self.core_graph(A, B, b, N, C)
+        return C, {"N": N, "p": p, "preq": preq}
+
+    def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, graph=False, prof=None, seed=0, config=None,
+            force_p=None):
+        """C = A B in emulated FP64; returns (C, info).  ``config`` ({'N':.., 'p':..}, e.g. from pick_config) overrides
+        the a-priori rule (ozaki_engine.py:1460-1505)."""
+        if config is not None:
+            force_N, force_p = int(config["N"]), config.get("p")
+        self._shape_check(A, B, C)
+        m, k = A.shape
+        n = B.shape[1]
+        if graph:
+            if C is None:
+                C = torch.empty(m, n, dtype=torch.float64, device=DEV)
+            return self.run_fast(A, B, C, tau=tau, inside=inside, force_N=force_N, force_p=force_p)
+        b = self.buffers(m, n, k, force_N or 20)
+        if C is None:
+            C = torch.empty(m, n, dtype=torch.float64, device=DEV)
+        t0 = time.perf_counter()
+        if prof is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self.stats(A, B, b, inside)
+        if prof is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+        N, p, info, h = self.choose(A, B, b, tau, force_N, seed, prof=prof)
+        if prof is not None:
+            prof["stats_gpu"] = e0.elapsed_time(e1) / 1e3
+            prof["stats+rule_wall"] = time.perf_counter() - t0
+        if N is None:
+            info["fallback"] = True
+            torch.matmul(A, B, out=C)
+            return C, info
+        if b["N"] < N:
+            b = self.buffers(m, n, k, N)                   # grow (statistics are recomputed)
+            self.stats(A, B, b, inside)
+        if force_p is not None:
+            if force_p > p:                                # unsafe table entry for this data: native fallback
+                info["fallback"] = True
+                info["config_rejected"] = True
+                torch.matmul(A, B, out=C)
+                return C, info
+            p = int(force_p)
+        b["pdev"].fill_(p)
+        info.update({"N": N, "p": p, "L": limbs_for(N), "stats": h})
+        if graph:
+            self.core_graph(A, B, b, N, C)
+        else:
+            self.core(A, B, b, N, C, prof=prof)
+        return C, info
+
+
+__all__ = ["OzakiCRT", "DEV", "MODS", "NMAX", "NEG", "pmax_bits"]

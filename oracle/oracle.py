@@ -1,0 +1,277 @@
+"""CPU oracle for the FP64-on-INT8 (Ozaki-II / CRT) GEMM path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and the cpu_baseline / reference arm of ``bench.py`` import this module,
+and only as the checker (or, in bench.py, as the timed CPU baseline).  The product package never imports it.
+
+It wraps ``libozaki_oracle.so`` (``ozaki_oracle.c``: a C/OpenMP restatement of the reference engine
+dl1683/matrix-numbers ``code/ozaki_engine.py``, file:line citations in that file) with numpy-level functions, and
+adds the pieces of the reference's host logic that are plain Python there:
+
+* ``probe_sets``          -- the probe rows/columns of ``choose`` (ozaki_engine.py:1265-1273)
+* ``rule``                -- the host form of the a-priori rule (ozaki_engine.py:1250-1307), computed in C
+* ``run``                 -- stats -> rule -> core, the eager ``OzakiCRT.run`` (ozaki_engine.py:1460-1505)
+
+The oracle is pinned against the reference itself by ``tests/test_oracle_golden.py`` (golden vectors generated
+by ``tests/golden/make_golden.py`` from the reference's own ``np_stats``, ``expected_core``, ``pmax_bits``,
+``choose`` and ``_rule_device``).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libozaki_oracle.so")
+
+MODS = [256, 255, 253, 251, 247, 241, 239, 233, 229, 227, 223, 217, 211, 199, 197, 193, 191, 181, 179, 173, 167, 163,
+        157, 151, 149, 139, 137, 131, 127, 113, 109, 107]
+NMAX = 32
+NEG = -1000000
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile libozaki_oracle.so with the committed Makefile (gcc, OpenMP)."""
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(
+            os.path.join(HERE, "ozaki_oracle.c")):
+        subprocess.run(["make", "-C", HERE, "-s"], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.c_void_p
+        i32, f64 = ctypes.c_int, ctypes.c_double
+        L.ozo_stats.argtypes = [P, P, i32, i32, i32, i32, P, P, P, P, P, P, P, P]
+        L.ozo_pmax_bits.argtypes = [i32, f64, f64, i32]
+        L.ozo_pmax_bits.restype = i32
+        L.ozo_modulus_product.argtypes = [i32]
+        L.ozo_modulus_product.restype = f64
+        L.ozo_limbs_for.argtypes = [i32]
+        L.ozo_limbs_for.restype = i32
+        L.ozo_probe_D.argtypes = [P, P, i32, i32, i32, P, i32, P, i32, P]
+        L.ozo_rule.argtypes = [P, P, P, P, P, P, i32, i32, i32, i32, P, i32, P, i32, P, f64, f64, i32, P, P, P]
+        L.ozo_split_A.argtypes = [P, P, P, i32, i32, i32, i32, P]
+        L.ozo_split_B.argtypes = [P, P, P, i32, i32, i32, i32, P]
+        L.ozo_gemm_mod.argtypes = [P, P, i32, i32, i32, i32, P]
+        L.ozo_gemm_i32.argtypes = [P, P, i32, i32, i32, P]
+        L.ozo_recon.argtypes = [P, P, P, i32, i32, i32, i32, P]
+        L.ozo_core.argtypes = [P, P, P, P, P, i32, i32, i32, i32, i32, P]
+        L.ozo_core.restype = i32
+        L.ozo_num_threads.restype = i32
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def _c64(a):
+    return np.ascontiguousarray(a, dtype=np.float64)
+
+
+def num_threads() -> int:
+    return int(lib().ozo_num_threads())
+
+
+def stats(A, B, inside=True):
+    """Reference statistics (ozaki_engine.py:846-951): dict gam, r, c, sA, nA, sB, nB, flag."""
+    A, B = _c64(A), _c64(B)
+    m, k = A.shape
+    n = B.shape[1]
+    out = {"gam": np.zeros(k, np.int32), "r": np.zeros(m, np.int32), "c": np.zeros(n, np.int32),
+           "sA": np.zeros(m), "nA": np.zeros(m), "sB": np.zeros(n), "nB": np.zeros(n)}
+    flag = np.zeros(1, np.int32)
+    lib().ozo_stats(_p(A), _p(B), m, n, k, 1 if inside else 0, _p(out["gam"]), _p(out["r"]), _p(out["c"]),
+                    _p(out["sA"]), _p(out["nA"]), _p(out["sB"]), _p(out["nB"]), _p(flag))
+    out["flag"] = int(flag[0])
+    return out
+
+
+def pmax_bits(N, nuA, nuB, k) -> int:
+    return int(lib().ozo_pmax_bits(int(N), float(nuA), float(nuB), int(k)))
+
+
+def modulus_product(N) -> float:
+    return float(lib().ozo_modulus_product(int(N)))
+
+
+def limbs_for(N) -> int:
+    return int(lib().ozo_limbs_for(int(N)))
+
+
+def probe_random(m, n, seed=0):
+    """Random part of the probe set: RandomState(seed).choice without replacement, rows then columns
+    (ozaki_engine.py:1265-1267 and :1399-1401)."""
+    rs = np.random.RandomState(seed)
+    Ir = rs.choice(m, min(64, m), replace=False)
+    Jr = rs.choice(n, min(64, n), replace=False)
+    return Ir.astype(np.int64), Jr.astype(np.int64)
+
+
+def hard_top(r, s, k, count=32):
+    """Indices of the `count` largest 2^r k / s (0 where s == 0); ties broken by the lower index
+    (ozaki_engine.py:1268-1271)."""
+    r = np.asarray(r, dtype=np.float64)
+    s = np.asarray(s, dtype=np.float64)
+    with np.errstate(all="ignore"):
+        h = np.where(s > 0, np.exp2(r) * k / s, 0.0)
+    order = np.argsort(-h, kind="stable")
+    return order[:min(count, len(h))].astype(np.int64)
+
+
+def probe_sets(st, m, n, k, seed=0):
+    Ir, Jr = probe_random(m, n, seed)
+    I = np.unique(np.concatenate([Ir, hard_top(st["r"], st["sA"], k)]))
+    J = np.unique(np.concatenate([Jr, hard_top(st["c"], st["sB"], k)]))
+    return I.astype(np.int64), J.astype(np.int64)
+
+
+def probe_D(A, B, I, J):
+    A, B = _c64(A), _c64(B)
+    m, k = A.shape
+    n = B.shape[1]
+    I = np.ascontiguousarray(I, dtype=np.int64)
+    J = np.ascontiguousarray(J, dtype=np.int64)
+    D = np.zeros((len(I), len(J)))
+    lib().ozo_probe_D(_p(A), _p(B), m, n, k, _p(I), len(I), _p(J), len(J), _p(D))
+    return D
+
+
+def rule(st, m, n, k, I, J, D, tau=2.0 ** -52, safety=2.0, force_N=None):
+    """Host form of the a-priori rule given stats, probe sets and D (ozaki_engine.py:1250-1307).
+    Returns dict N (None on fallback), p, fallback, p_req, worst_ratio_E_over_D, nuA, nuB."""
+    I = np.ascontiguousarray(I, dtype=np.int64)
+    J = np.ascontiguousarray(J, dtype=np.int64)
+    D = _c64(D)
+    out = np.zeros(4, np.int32)
+    worst = np.zeros(1)
+    nus = np.zeros(2)
+    r = np.ascontiguousarray(st["r"], np.int32)
+    c = np.ascontiguousarray(st["c"], np.int32)
+    sA, sB, nA, nB = (_c64(st[x]) for x in ("sA", "sB", "nA", "nB"))
+    lib().ozo_rule(_p(r), _p(c), _p(sA), _p(sB), _p(nA), _p(nB), m, n, k, int(st.get("flag", 0)), _p(I), len(I), _p(J),
+                   len(J), _p(D), float(tau), float(safety), int(force_N or 0), _p(out), _p(worst), _p(nus))
+    return {"N": int(out[0]) if out[0] else None, "p": int(out[1]), "fallback": bool(out[2]), "p_req": int(out[3]),
+            "worst_ratio_E_over_D": float(worst[0]), "nuA": float(nus[0]), "nuB": float(nus[1])}
+
+
+def split_A(A, r, gam, p, N):
+    A = _c64(A)
+    m, k = A.shape
+    out = np.zeros((N, m, k), np.int8)
+    lib().ozo_split_A(_p(A), _p(np.ascontiguousarray(r, np.int32)), _p(np.ascontiguousarray(gam, np.int32)), m, k,
+                      int(p), int(N), _p(out))
+    return out
+
+
+def split_B(B, c, gam, p, N):
+    B = _c64(B)
+    k, n = B.shape
+    out = np.zeros((N, n, k), np.int8)
+    lib().ozo_split_B(_p(B), _p(np.ascontiguousarray(c, np.int32)), _p(np.ascontiguousarray(gam, np.int32)), k, n,
+                      int(p), int(N), _p(out))
+    return out
+
+
+def gemm_mod(Ares, Bres):
+    N, m, k = Ares.shape
+    n = Bres.shape[1]
+    X = np.zeros((N, m, n), np.uint8)
+    lib().ozo_gemm_mod(_p(np.ascontiguousarray(Ares)), _p(np.ascontiguousarray(Bres)), m, n, k, N, _p(X))
+    return X
+
+
+def gemm_i32(At, Bt):
+    m, k = At.shape
+    n = Bt.shape[0]
+    C = np.zeros((m, n), np.int32)
+    lib().ozo_gemm_i32(_p(np.ascontiguousarray(At)), _p(np.ascontiguousarray(Bt)), m, n, k, _p(C))
+    return C
+
+
+def recon(X, r, c, p):
+    N, m, n = X.shape
+    C = np.zeros((m, n))
+    lib().ozo_recon(_p(np.ascontiguousarray(X)), _p(np.ascontiguousarray(r, np.int32)),
+                    _p(np.ascontiguousarray(c, np.int32)), m, n, N, int(p), _p(C))
+    return C
+
+
+def core(A, B, st, N, p):
+    """split + exact products + reconstruction for given (N, p): the CPU port of core() (ozaki_engine.py:1310)."""
+    A, B = _c64(A), _c64(B)
+    m, k = A.shape
+    n = B.shape[1]
+    C = np.zeros((m, n))
+    rc = lib().ozo_core(_p(A), _p(B), _p(np.ascontiguousarray(st["gam"], np.int32)),
+                        _p(np.ascontiguousarray(st["r"], np.int32)), _p(np.ascontiguousarray(st["c"], np.int32)),
+                        m, n, k, int(N), int(p), _p(C))
+    if rc != 0:
+        raise MemoryError("oracle core: allocation failed")
+    return C
+
+
+def run(A, B, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, safety=2.0):
+    """Eager OzakiCRT.run on the CPU (ozaki_engine.py:1460-1505): returns (C, info).  Fallback cases return
+    C = None (the reference would call native DGEMM there)."""
+    A, B = _c64(A), _c64(B)
+    m, k = A.shape
+    n = B.shape[1]
+    st = stats(A, B, inside)
+    info = {"nonfinite": bool(st["flag"])}
+    if st["flag"]:
+        info["fallback"] = True
+        return None, info
+    I, J = probe_sets(st, m, n, k, seed)
+    D = probe_D(A, B, I, J) if not force_N else np.zeros((len(I), len(J)))
+    ru = rule(st, m, n, k, I, J, D, tau, safety, force_N)
+    info.update(ru)
+    info["probe"] = [len(I), len(J)]
+    if ru["fallback"] or ru["N"] is None:
+        info["fallback"] = True
+        return None, info
+    N, p = ru["N"], ru["p"]
+    if force_p is not None:
+        if force_p > p:
+            info["fallback"] = True
+            info["config_rejected"] = True
+            return None, info
+        p = int(force_p)
+    info["N"], info["p"], info["L"] = N, p, limbs_for(N)
+    info["stats"] = st
+    return core(A, B, st, N, p), info
+
+
+# ------------------------------------------------------------------ the exact sampled reference (measurement)
+def _split(a):
+    t = 134217729.0 * a
+    hi = t - (t - a)
+    return hi, a - hi
+
+
+def exact_sample(Ar, Bc):
+    """Correctly rounded Ar @ Bc by Dekker TwoProduct + math.fsum (the reference's exact_sample,
+    ozaki_engine.py:477-496)."""
+    r, n = Ar.shape
+    c = Bc.shape[1]
+    out = np.empty((r, c))
+    bh, bl = _split(Bc)
+    for i in range(r):
+        a = Ar[i][:, None]
+        ah, al = _split(a)
+        p = a * Bc
+        e = ((ah * bh - p) + ah * bl + al * bh) + al * bl
+        for j in range(c):
+            out[i, j] = math.fsum(p[:, j].tolist() + e[:, j].tolist())
+    return out
