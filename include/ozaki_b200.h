@@ -70,6 +70,14 @@ int ozk_stats(const double* A, const double* B, int m, int n, int k, int inside,
               int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag, void* workspace,
               size_t workspace_bytes, ozk_stream_t stream);
 
+/* Stage 1 in two phases, for C row blocks spread over several GPUs (the column max of |A| is all-reduced with MAX
+ * between them): colmax[k] = max_i |A_il| as IEEE bit patterns (the reference's colmax_k, :847-854), then the rest
+ * of stage 1 given the (global) colmax.  ozk_stats == ozk_stats_colmax + ozk_stats_finish.                  */
+int ozk_stats_colmax(const double* A, int m, int k, uint64_t* colmax, ozk_stream_t stream);
+int ozk_stats_finish(const double* A, const double* B, int m, int n, int k, int inside, const uint64_t* colmax,
+                     int32_t* gam, int32_t* r, int32_t* c, double* sA, double* nA, double* sB, double* nB,
+                     int32_t* flag, void* workspace, size_t workspace_bytes, ozk_stream_t stream);
+
 /* ---- stage 2: the a-priori plane-count rule on the device (replaces OzakiCRT.choose, ozaki_engine.py:
  * 1250-1307, and OzakiCRT._rule_device, :1372-1426).  probe_rows / probe_cols: the random part of the probe
  * set (RandomState(seed).choice, :1265-1267), device int64; the 32 "hard" rows and columns are added on the
@@ -83,6 +91,24 @@ int ozk_rule(const double* A, const double* B, int m, int n, int k, const int32_
              const int64_t* probe_rows, int n_probe_rows, const int64_t* probe_cols, int n_probe_cols, double tau,
              double safety, int force_N, int force_p, int32_t* dec, int32_t* p_dev, double* aux, void* workspace,
              size_t workspace_bytes, ozk_stream_t stream);
+
+/* Stage 2 in three phases, for C row blocks spread over several GPUs: ozk_rule == prepare + probe + finish.
+ * prepare: nu, pv, forced / non-finite decisions and the probe sets (r, sA, nA over ALL m rows);
+ * probe:   the probe product D = |A_I| |B_J| restricted to the probe rows inside [row_begin, row_begin + rows),
+ *          A_rows pointing at that row block (other rows give 0); D (96 x 96 doubles, row-major, padded) sits at
+ *          byte offset ozk_rule_probe_offset() of the workspace, where the callers sum the blocks' D matrices;
+ * finish:  p_req, N, p and the outputs of ozk_rule from D.                                                    */
+size_t ozk_rule_probe_offset(int m, int n, int k);
+int ozk_rule_prepare(const int32_t* r, const int32_t* c, const double* sA, const double* nA, const double* sB,
+                     const double* nB, const int32_t* flag, int m, int n, int k, const int64_t* probe_rows,
+                     int n_probe_rows, const int64_t* probe_cols, int n_probe_cols, int force_N, int force_p,
+                     int32_t* dec, int32_t* p_dev, double* aux, void* workspace, size_t workspace_bytes,
+                     ozk_stream_t stream);
+int ozk_rule_probe(const double* A_rows, const double* B, int row_begin, int rows, int m, int n, int k,
+                   void* workspace, size_t workspace_bytes, ozk_stream_t stream);
+int ozk_rule_finish(const int32_t* r, const int32_t* c, const double* sA, const double* sB, int m, int n, int k,
+                    double tau, double safety, int32_t* dec, int32_t* p_dev, double* aux, void* workspace,
+                    size_t workspace_bytes, ozk_stream_t stream);
 
 /* ---- stage 3a: residue split (replaces resA_k / resB_k, ozaki_engine.py:996-1038 and :1328-1331) --------- *
  * Ares[t][i][l] = symmetric residue of round(A_il 2^(p - r_i + gam_l)) modulo m_t, t < N, as int8;

@@ -31,7 +31,13 @@ _SIGNATURES = {
     "ozk_pmax_bits": ([I32, F64, F64, I32], I32),
     "ozk_stats_workspace_bytes": ([I32, I32, I32], SZ),
     "ozk_stats": ([P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, SZ, P], I32),
+    "ozk_stats_colmax": ([P, I32, I32, P, P], I32),
+    "ozk_stats_finish": ([P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, SZ, P], I32),
     "ozk_rule_workspace_bytes": ([I32, I32, I32], SZ),
+    "ozk_rule_probe_offset": ([I32, I32, I32], SZ),
+    "ozk_rule_prepare": ([P, P, P, P, P, P, P, I32, I32, I32, P, I32, P, I32, I32, I32, P, P, P, P, SZ, P], I32),
+    "ozk_rule_probe": ([P, P, I32, I32, I32, I32, I32, P, SZ, P], I32),
+    "ozk_rule_finish": ([P, P, P, P, I32, I32, I32, F64, F64, P, P, P, P, SZ, P], I32),
     "ozk_rule": ([P, P, I32, I32, I32, P, P, P, P, P, P, P, P, I32, P, I32, F64, F64, I32, I32, P, P, P, P, SZ, P], I32),
     "ozk_split_a": ([P, P, P, P, I32, I32, I32, P, P], I32),
     "ozk_split_b": ([P, P, P, P, I32, I32, I32, P, P], I32),

@@ -73,12 +73,13 @@ __device__ __forceinline__ double to_double_unscaled(double (&a)[C], int scale_e
         else if (c == ct - 2) lo = v;
         else if (c < ct - 2) sticky |= v != 0ULL;
     }
-    // V = h 2^80 + md 2^40 + lo (120 bits), top 64 bits + sticky
+    // V = h 2^80 + md 2^40 + lo; h (1 <= h < 2^40) has 64 - lz bits, so V has 144 - lz bits and its top 64 bits
+    // are V >> (80 - lz), with 17 <= 80 - lz <= 56; the bits shifted out and the lower chunks form the sticky bit
     const unsigned __int128 V = ((unsigned __int128)h << 80) | ((unsigned __int128)md << 40) | (unsigned __int128)lo;
-    const int lz = __clzll((long long)h);                 // >= 24
-    const int shift = max(0, 56 - lz);
+    const int lz = __clzll((long long)h);
+    const int shift = 80 - lz;
     unsigned long long qv = (unsigned long long)(V >> shift);
-    const unsigned __int128 mask = shift ? ((((unsigned __int128)1) << shift) - 1) : (unsigned __int128)0;
+    const unsigned __int128 mask = (((unsigned __int128)1) << shift) - 1;
     if (sticky || (V & mask) != 0) qv |= 1ULL;
     const double d = __ull2double_rn(qv);
     return ldexp(d, shift + 40 * (ct - 2) + scale_exp);

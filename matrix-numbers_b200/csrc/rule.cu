@@ -181,8 +181,11 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
 }
 
 // split-K probe product: partial[b][a][j] = sum over this block's contraction tiles of |A_I[a] l| |B_l J[j]|
+// A holds rows [row_begin, row_begin + rows) of the full matrix; probe rows outside it contribute zeros (another
+// GPU's block supplies them; the callers sum the D matrices of all blocks)
 __global__ void __launch_bounds__(kProbeThreads) probe_partial_kernel(const double* __restrict__ A, const double* __restrict__ B,
-                                                                      int n, int k, const RuleCtl* __restrict__ ctl,
+                                                                      int row_begin, int rows, int n, int k,
+                                                                      const RuleCtl* __restrict__ ctl,
                                                                       double* __restrict__ partial) {
     if (ctl->done) return;
     __shared__ double sa[kProbeMax][kProbeK + 1];
@@ -190,7 +193,8 @@ __global__ void __launch_bounds__(kProbeThreads) probe_partial_kernel(const doub
     __shared__ int sI[kProbeMax], sJ[kProbeMax];
     const int nI = ctl->nI, nJ = ctl->nJ;
     for (int x = threadIdx.x; x < kProbeMax; x += blockDim.x) {
-        sI[x] = x < nI ? ctl->I[x] : -1;
+        const int gi = x < nI ? ctl->I[x] - row_begin : -1;
+        sI[x] = (gi >= 0 && gi < rows) ? gi : -1;
         sJ[x] = x < nJ ? ctl->J[x] : -1;
     }
     const int a0 = (threadIdx.x >> 4) * 6, b0 = (threadIdx.x & 15) * 6;
@@ -346,21 +350,26 @@ int probe_blocks(int k) {
     return max(1, min(tiles, 2 * sms));
 }
 
+size_t ctl_bytes() { return (sizeof(RuleCtl) + 255) & ~(size_t)255; }
+
 }  // namespace
 
 extern "C" size_t ozk_rule_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
-    const size_t ctl = (sizeof(RuleCtl) + 255) & ~(size_t)255;
-    return ctl + (size_t)(probe_blocks(k) + 1) * kProbeMax * kProbeMax * sizeof(double);
+    return ctl_bytes() + (size_t)(probe_blocks(k) + 1) * kProbeMax * kProbeMax * sizeof(double);
 }
 
-extern "C" int ozk_rule(const double* A, const double* B, int m, int n, int k, const int32_t* r, const int32_t* c,
-                        const double* sA, const double* nA, const double* sB, const double* nB, const int32_t* flag,
-                        const int64_t* probe_rows, int n_probe_rows, const int64_t* probe_cols, int n_probe_cols,
-                        double tau, double safety, int force_N, int force_p, int32_t* dec, int32_t* p_dev, double* aux,
-                        void* workspace, size_t workspace_bytes, ozk_stream_t stream_) {
-    if (!A || !B || !r || !c || !sA || !nA || !sB || !nB || !flag || !dec || !p_dev || !aux || !workspace)
-        return OZK_ERR_ARG;
+extern "C" size_t ozk_rule_probe_offset(int m, int n, int k) {
+    if (m <= 0 || n <= 0 || k <= 0) return 0;
+    return ctl_bytes() + (size_t)probe_blocks(k) * kProbeMax * kProbeMax * sizeof(double);
+}
+
+extern "C" int ozk_rule_prepare(const int32_t* r, const int32_t* c, const double* sA, const double* nA, const double* sB,
+                                const double* nB, const int32_t* flag, int m, int n, int k, const int64_t* probe_rows,
+                                int n_probe_rows, const int64_t* probe_cols, int n_probe_cols, int force_N, int force_p,
+                                int32_t* dec, int32_t* p_dev, double* aux, void* workspace, size_t workspace_bytes,
+                                ozk_stream_t stream_) {
+    if (!r || !c || !sA || !nA || !sB || !nB || !flag || !dec || !p_dev || !aux || !workspace) return OZK_ERR_ARG;
     if (m <= 0 || n <= 0 || k <= 0) return OZK_ERR_ARG;
     if (force_N != 0 && (force_N < 1 || force_N > OZK_NMAX)) return OZK_ERR_ARG;
     if (force_N == 0) {
@@ -372,18 +381,53 @@ extern "C" int ozk_rule(const double* A, const double* B, int m, int n, int k, c
     MTable mt;
     for (int N = 0; N <= OZK_NMAX; N++) mt.M[N] = N ? ozk_modulus_product(N) : 1.0;
     RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
-    double* partial = reinterpret_cast<double*>(static_cast<char*>(workspace) + ((sizeof(RuleCtl) + 255) & ~(size_t)255));
-    const int nb = probe_blocks(k);
     rule_prep_kernel<<<1, kPrepThreads, 0, st>>>(r, c, sA, nA, sB, nB, flag, probe_rows, n_probe_rows, probe_cols,
                                                  n_probe_cols, m, n, k, force_N, force_N > 0 ? force_p : -1, mt, ctl, dec,
                                                  p_dev, aux);
     OZK_CHECK_LAUNCH();
-    probe_partial_kernel<<<nb, kProbeThreads, 0, st>>>(A, B, n, k, ctl, partial);
+    return OZK_OK;
+}
+
+extern "C" int ozk_rule_probe(const double* A_rows, const double* B, int row_begin, int rows, int m, int n, int k,
+                              void* workspace, size_t workspace_bytes, ozk_stream_t stream_) {
+    if (!A_rows || !B || !workspace) return OZK_ERR_ARG;
+    if (m <= 0 || n <= 0 || k <= 0 || rows <= 0 || row_begin < 0 || row_begin + rows > m) return OZK_ERR_ARG;
+    if (workspace_bytes < ozk_rule_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
+    double* partial = reinterpret_cast<double*>(static_cast<char*>(workspace) + ctl_bytes());
+    const int nb = probe_blocks(k);
+    probe_partial_kernel<<<nb, kProbeThreads, 0, st>>>(A_rows, B, row_begin, rows, n, k, ctl, partial);
     OZK_CHECK_LAUNCH();
     double* D = partial + (size_t)nb * kProbeMax * kProbeMax;
     probe_reduce_kernel<<<(kProbeMax * kProbeMax + 255) / 256, 256, 0, st>>>(partial, nb, ctl, D);
     OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}
+
+extern "C" int ozk_rule_finish(const int32_t* r, const int32_t* c, const double* sA, const double* sB, int m, int n,
+                               int k, double tau, double safety, int32_t* dec, int32_t* p_dev, double* aux,
+                               void* workspace, size_t workspace_bytes, ozk_stream_t stream_) {
+    if (!r || !c || !sA || !sB || !dec || !p_dev || !aux || !workspace) return OZK_ERR_ARG;
+    if (m <= 0 || n <= 0 || k <= 0) return OZK_ERR_ARG;
+    if (workspace_bytes < ozk_rule_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
+    const double* D = reinterpret_cast<const double*>(static_cast<char*>(workspace) + ozk_rule_probe_offset(m, n, k));
     rule_final_kernel<<<1, kFinalThreads, 0, st>>>(r, c, sA, sB, k, tau, safety, D, ctl, dec, p_dev, aux);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
+}
+
+extern "C" int ozk_rule(const double* A, const double* B, int m, int n, int k, const int32_t* r, const int32_t* c,
+                        const double* sA, const double* nA, const double* sB, const double* nB, const int32_t* flag,
+                        const int64_t* probe_rows, int n_probe_rows, const int64_t* probe_cols, int n_probe_cols,
+                        double tau, double safety, int force_N, int force_p, int32_t* dec, int32_t* p_dev, double* aux,
+                        void* workspace, size_t workspace_bytes, ozk_stream_t stream) {
+    if (!A || !B) return OZK_ERR_ARG;
+    int rc = ozk_rule_prepare(r, c, sA, nA, sB, nB, flag, m, n, k, probe_rows, n_probe_rows, probe_cols, n_probe_cols,
+                              force_N, force_p, dec, p_dev, aux, workspace, workspace_bytes, stream);
+    if (rc != OZK_OK) return rc;
+    if ((rc = ozk_rule_probe(A, B, 0, m, m, n, k, workspace, workspace_bytes, stream)) != OZK_OK) return rc;
+    return ozk_rule_finish(r, c, sA, sB, m, n, k, tau, safety, dec, p_dev, aux, workspace, workspace_bytes, stream);
 }

@@ -196,28 +196,36 @@ extern "C" size_t ozk_stats_workspace_bytes(int m, int n, int k) {
     return align256((size_t)k * 8) * 2 + align256(nchunks * (size_t)n * 8) * 2;
 }
 
-extern "C" int ozk_stats(const double* A, const double* B, int m, int n, int k, int inside, int32_t* gam, int32_t* r,
-                         int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag, void* workspace,
-                         size_t workspace_bytes, ozk_stream_t stream_) {
-    if (!A || !B || !gam || !r || !c || !sA || !nA || !sB || !nB || !flag || !workspace) return OZK_ERR_ARG;
+extern "C" int ozk_stats_colmax(const double* A, int m, int k, uint64_t* colmax, ozk_stream_t stream_) {
+    if (!A || !colmax) return OZK_ERR_ARG;
+    if (m <= 0 || k <= 0 || (k & 1)) return OZK_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(A) & 15) return OZK_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    if (cudaMemsetAsync(colmax, 0, (size_t)k * 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
+    colmax_a_kernel<<<dim3((k / 2 + kThreads - 1) / kThreads, (m + kColmaxRows - 1) / kColmaxRows), kThreads, 0, st>>>(
+        A, reinterpret_cast<unsigned long long*>(colmax), m, k);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}
+
+extern "C" int ozk_stats_finish(const double* A, const double* B, int m, int n, int k, int inside, const uint64_t* colmax,
+                                int32_t* gam, int32_t* r, int32_t* c, double* sA, double* nA, double* sB, double* nB,
+                                int32_t* flag, void* workspace, size_t workspace_bytes, ozk_stream_t stream_) {
+    if (!A || !B || !colmax || !gam || !r || !c || !sA || !nA || !sB || !nB || !flag || !workspace) return OZK_ERR_ARG;
     if (m <= 0 || n <= 0 || k <= 0 || (k & 1) || (n & 1)) return OZK_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return OZK_ERR_ARG;
     if (workspace_bytes < ozk_stats_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
     const int nchunks = (k + kColChunk - 1) / kColChunk;
     char* ws = static_cast<char*>(workspace);
-    unsigned long long* colmax = reinterpret_cast<unsigned long long*>(ws);
     unsigned long long* rowmax = reinterpret_cast<unsigned long long*>(ws + align256((size_t)k * 8));
     double* ps = reinterpret_cast<double*>(ws + 2 * align256((size_t)k * 8));
     double* pq = reinterpret_cast<double*>(ws + 2 * align256((size_t)k * 8) + align256((size_t)nchunks * n * 8));
-
-    if (cudaMemsetAsync(colmax, 0, (size_t)k * 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
     if (cudaMemsetAsync(flag, 0, 4, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
-    colmax_a_kernel<<<dim3((k / 2 + kThreads - 1) / kThreads, (m + kColmaxRows - 1) / kColmaxRows), kThreads, 0, st>>>(A, colmax, m, k);
-    OZK_CHECK_LAUNCH();
     rowmax_b_kernel<<<k, kThreads, 0, st>>>(B, rowmax, n);
     OZK_CHECK_LAUNCH();
-    gamma_kernel<<<(k + 255) / 256, 256, 0, st>>>(colmax, rowmax, gam, flag, k, inside ? 1 : 0);
+    gamma_kernel<<<(k + 255) / 256, 256, 0, st>>>(reinterpret_cast<const unsigned long long*>(colmax), rowmax, gam, flag,
+                                                  k, inside ? 1 : 0);
     OZK_CHECK_LAUNCH();
     rowstats_a_kernel<<<m, kThreads, 0, st>>>(A, gam, k, r, sA, nA);
     OZK_CHECK_LAUNCH();
@@ -231,4 +239,15 @@ extern "C" int ozk_stats(const double* A, const double* B, int m, int n, int k, 
     colsums_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(ps, pq, nchunks, n, c, sB, nB);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
+}
+
+extern "C" int ozk_stats(const double* A, const double* B, int m, int n, int k, int inside, int32_t* gam, int32_t* r,
+                         int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag, void* workspace,
+                         size_t workspace_bytes, ozk_stream_t stream) {
+    if (!workspace || workspace_bytes < ozk_stats_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
+    uint64_t* colmax = static_cast<uint64_t*>(workspace);   // the first region of the workspace
+    int rc = ozk_stats_colmax(A, m, k, colmax, stream);
+    if (rc != OZK_OK) return rc;
+    return ozk_stats_finish(A, B, m, n, k, inside, colmax, gam, r, c, sA, nA, sB, nB, flag, workspace, workspace_bytes,
+                            stream);
 }
