@@ -52,6 +52,8 @@ def lib():
         P = ctypes.c_void_p
         i32, f64 = ctypes.c_int, ctypes.c_double
         L.ozo_stats.argtypes = [P, P, i32, i32, i32, i32, P, P, P, P, P, P, P, P]
+        L.ozo_stats_ext.argtypes = [P, P, i32, i32, i32, i32, P, P, P, P, P, P, P, P, P]
+        L.ozo_colmax.argtypes = [P, i32, i32, P]
         L.ozo_pmax_bits.argtypes = [i32, f64, f64, i32]
         L.ozo_pmax_bits.restype = i32
         L.ozo_modulus_product.argtypes = [i32]
@@ -94,6 +96,30 @@ def stats(A, B, inside=True):
     flag = np.zeros(1, np.int32)
     lib().ozo_stats(_p(A), _p(B), m, n, k, 1 if inside else 0, _p(out["gam"]), _p(out["r"]), _p(out["c"]),
                     _p(out["sA"]), _p(out["nA"]), _p(out["sB"]), _p(out["nB"]), _p(flag))
+    out["flag"] = int(flag[0])
+    return out
+
+
+def colmax(A):
+    """max over rows of the |A_il| bit patterns (uint64 as int64)."""
+    A = _c64(A)
+    m, k = A.shape
+    out = np.zeros(k, np.uint64)
+    lib().ozo_colmax(_p(A), m, k, _p(out))
+    return out.view(np.int64)
+
+
+def stats_given_colmax(A, B, colmax_global, inside=True):
+    """Statistics of a row block of A given the column max of |A| over all rows (row-sharded products)."""
+    A, B = _c64(A), _c64(B)
+    m, k = A.shape
+    n = B.shape[1]
+    cm = np.ascontiguousarray(np.asarray(colmax_global).view(np.uint64))
+    out = {"gam": np.zeros(k, np.int32), "r": np.zeros(m, np.int32), "c": np.zeros(n, np.int32),
+           "sA": np.zeros(m), "nA": np.zeros(m), "sB": np.zeros(n), "nB": np.zeros(n)}
+    flag = np.zeros(1, np.int32)
+    lib().ozo_stats_ext(_p(A), _p(B), m, n, k, 1 if inside else 0, _p(cm), _p(out["gam"]), _p(out["r"]), _p(out["c"]),
+                        _p(out["sA"]), _p(out["nA"]), _p(out["sB"]), _p(out["nB"]), _p(flag))
     out["flag"] = int(flag[0])
     return out
 
