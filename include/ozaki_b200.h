@@ -39,6 +39,7 @@ typedef void* ozk_stream_t;
 #define OZK_ERR_DEVICE (-3)       /* no CUDA device, or the device is not sm_100                            */
 #define OZK_ERR_DRIVER (-4)       /* driver entry point or TMA tensor-map encoding failed                   */
 #define OZK_ERR_WORKSPACE (-5)    /* workspace smaller than the *_workspace_bytes query                     */
+#define OZK_ERR_TOO_LARGE (-6)    /* problem needs more scratch than ozk_stats_noalloc's static array holds  */
 #define OZK_ERR_CUDA_BASE 1000    /* OZK_ERR_CUDA_BASE + cudaError_t of a failed launch or attribute call  */
 
 #define OZK_DEVERR_TIMEOUT_PRODUCER 1   /* GEMM: the TMA producer's bounded wait ran out   */
@@ -77,6 +78,19 @@ int ozk_stats_colmax(const double* A, int m, int k, uint64_t* colmax, ozk_stream
 int ozk_stats_finish(const double* A, const double* B, int m, int n, int k, int inside, const uint64_t* colmax,
                      int32_t* gam, int32_t* r, int32_t* c, double* sA, double* nA, double* sB, double* nB,
                      int32_t* flag, void* workspace, size_t workspace_bytes, ozk_stream_t stream);
+
+/* Stage 1 without a workspace argument, for callers that cannot allocate device memory (they only hold device
+ * pointers handed to them by another runtime, or must not call cudaMalloc while they run or record a CUDA graph).
+ * This entry point has no counterpart in the reference.  Its scratch is a static device array of
+ * OZK_STATS_NOALLOC_MAX_BYTES (16 MiB) inside the library, held on every device that loads the library until the
+ * process exits; a problem with ozk_stats_workspace_bytes(m, n, k) above that size is rejected with
+ * OZK_ERR_TOO_LARGE before any launch (16 MiB covers m, n, k <= 16384 and m = n = 32768 with k = 8192).  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress) and must therefore come before any
+ * stream capture on that device.  All calls share the array: calls whose work overlaps on the GPU race, so the
+ * caller serialises them (one stream, or an event between streams).  Outputs equal ozk_stats's.             */
+#define OZK_STATS_NOALLOC_MAX_BYTES (16u << 20)
+int ozk_stats_noalloc(const double* A, const double* B, int m, int n, int k, int inside, int32_t* gam, int32_t* r,
+                      int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag, ozk_stream_t stream);
 
 /* ---- stage 2: the a-priori plane-count rule on the device (replaces OzakiCRT.choose, ozaki_engine.py:
  * 1250-1307, and OzakiCRT._rule_device, :1372-1426).  probe_rows / probe_cols: the random part of the probe

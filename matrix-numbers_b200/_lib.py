@@ -31,6 +31,7 @@ _SIGNATURES = {
     "ozk_pmax_bits": ([I32, F64, F64, I32], I32),
     "ozk_stats_workspace_bytes": ([I32, I32, I32], SZ),
     "ozk_stats": ([P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, SZ, P], I32),
+    "ozk_stats_noalloc": ([P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P], I32),
     "ozk_stats_colmax": ([P, I32, I32, P, P], I32),
     "ozk_stats_finish": ([P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, SZ, P], I32),
     "ozk_rule_workspace_bytes": ([I32, I32, I32], SZ),

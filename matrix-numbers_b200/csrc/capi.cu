@@ -48,6 +48,7 @@ extern "C" const char* ozk_error_string(int code) {
         case OZK_ERR_DEVICE: return "no CUDA device of compute capability 10.x (B200, sm_100) is current";
         case OZK_ERR_DRIVER: return "CUDA driver entry point or TMA tensor-map encoding failed";
         case OZK_ERR_WORKSPACE: return "workspace smaller than the size returned by the matching *_workspace_bytes query";
+        case OZK_ERR_TOO_LARGE: return "problem needs more scratch than the static array of ozk_stats_noalloc (16 MiB)";
         default: break;
     }
     if (code >= OZK_ERR_CUDA_BASE) return cudaGetErrorString((cudaError_t)(code - OZK_ERR_CUDA_BASE));

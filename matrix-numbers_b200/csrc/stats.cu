@@ -251,3 +251,38 @@ extern "C" int ozk_stats(const double* A, const double* B, int m, int n, int k, 
     return ozk_stats_finish(A, B, m, n, k, inside, colmax, gam, r, c, sA, nA, sB, nB, flag, workspace, workspace_bytes,
                             stream);
 }
+
+// ---- statistics without a caller-supplied workspace -------------------------------------------------------------
+// For callers that cannot allocate device memory: code that only receives raw device pointers from another runtime
+// (a solver or database plugin whose host owns every allocation), or code that must not call cudaMalloc in the middle
+// of its work (inside a real-time loop, or while it is recording a CUDA graph).  The scratch of the statistics lives
+// in the static array below instead of a workspace argument.  It exists once per device that loads this library and
+// stays allocated until the process exits; every call uses the same bytes, so calls whose work overlaps on the GPU
+// (different streams, or different host threads) race and must be serialised by the caller.
+namespace {
+
+__device__ __align__(256) unsigned char g_stats_scratch[OZK_STATS_NOALLOC_MAX_BYTES];
+
+void* g_stats_scratch_ptr[64];   // device address of g_stats_scratch, per device ordinal (set up on first use)
+
+}  // namespace
+
+extern "C" int ozk_stats_noalloc(const double* A, const double* B, int m, int n, int k, int inside, int32_t* gam,
+                                 int32_t* r, int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag,
+                                 ozk_stream_t stream) {
+    const size_t need = ozk_stats_workspace_bytes(m, n, k);
+    if (need == 0) return OZK_ERR_ARG;
+    if (need > (size_t)OZK_STATS_NOALLOC_MAX_BYTES) return OZK_ERR_TOO_LARGE;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return OZK_ERR_DEVICE;
+    if (!g_stats_scratch_ptr[dev]) {
+        // one-time set-up on this device (the current one): the host-side name of the array is not a device address
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_stats_scratch);
+        if (e != cudaSuccess || !p) return OZK_ERR_CUDA_BASE + (int)e;
+        g_stats_scratch_ptr[dev] = p;
+    }
+    // the statistics clear what must start at zero (the column maxima, the flag); everything else is overwritten
+    return ozk_stats(A, B, m, n, k, inside, gam, r, c, sA, nA, sB, nB, flag, g_stats_scratch_ptr[dev],
+                     (size_t)OZK_STATS_NOALLOC_MAX_BYTES, stream);
+}
