@@ -25,6 +25,7 @@ struct ReconParams {
     double Mc[kCMax + 1];        // chunks of M
     double Mh[kCMax + 1];        // chunks of M / 2
     double invM[kCMax + 1];      // 2^(40 c) / M
+    double P40[kCMax + 1];       // 2^(40 c)
     double Mf;                   // float(M)
     int N, C;
 };
@@ -55,41 +56,55 @@ __device__ __forceinline__ void sub_scaled(double (&a)[C], const double* b, doub
     normalize<C>(a);
 }
 
-template <int C>
-__device__ __forceinline__ double to_double_unscaled(double (&a)[C], int scale_exp) {
-    // a: normalised, non-negative; returns RN(a) * 2^scale_exp with the reference's two-step rounding
-    int ct = -1;
-#pragma unroll
-    for (int c = C - 1; c >= 0; c--)
-        if (ct < 0 && a[c] != 0.0) ct = c;
-    if (ct < 0) return 0.0;
-    unsigned long long h = 0, md = 0, lo = 0;
-    bool sticky = false;
-#pragma unroll
-    for (int c = 0; c < C; c++) {
-        const unsigned long long v = (unsigned long long)a[c];
-        if (c == ct) h = v;
-        else if (c == ct - 1) md = v;
-        else if (c == ct - 2) lo = v;
-        else if (c < ct - 2) sticky |= v != 0ULL;
-    }
-    // V = h 2^80 + md 2^40 + lo; h (1 <= h < 2^40) has 64 - lz bits, so V has 144 - lz bits and its top 64 bits
-    // are V >> (80 - lz), with 17 <= 80 - lz <= 56; the bits shifted out and the lower chunks form the sticky bit
-    const unsigned __int128 V = ((unsigned __int128)h << 80) | ((unsigned __int128)md << 40) | (unsigned __int128)lo;
-    const int lz = __clzll((long long)h);
-    const int shift = 80 - lz;
-    unsigned long long qv = (unsigned long long)(V >> shift);
-    const unsigned __int128 mask = (((unsigned __int128)1) << shift) - 1;
-    if (sticky || (V & mask) != 0) qv |= 1ULL;
-    const double d = __ull2double_rn(qv);
-    return ldexp(d, shift + 40 * (ct - 2) + scale_exp);
+// integer value of a chunk (an exact double in [0, 2^40)): the low mantissa bits of chunk + 2^52
+__device__ __forceinline__ unsigned long long chunk_bits(double v) {
+    return (unsigned long long)__double_as_longlong(v + 4503599627370496.0) & 0xfffffffffffffULL;
 }
 
 template <int C>
+__device__ __forceinline__ double to_double_unscaled(const double (&a)[C], int scale_exp) {
+    // a: normalised, non-negative; returns RN(a) * 2^scale_exp with the reference's two-step rounding
+    unsigned long long h = 0, md = 0, lo = 0;
+    int ct = -1;
+    bool sticky = false;
+#pragma unroll
+    for (int c = C - 1; c >= 0; c--) {
+        const unsigned long long v = chunk_bits(a[c]);
+        if (ct < 0) {
+            if (v != 0ULL) { ct = c; h = v; }
+        } else if (c == ct - 1) md = v;
+        else if (c == ct - 2) lo = v;
+        else sticky |= v != 0ULL;
+    }
+    if (ct < 0) return 0.0;
+    // value = (h 2^80 + md 2^40 + lo) 2^(40 (ct - 2)); t1 = its bits above the lowest 56 of the 120-bit window,
+    // nxt = those 56 bits left-aligned; normalise t1 (>= 2^24, so 0 <= sh <= 39) and keep a sticky bit
+    const unsigned long long t1 = (h << 24) | (md >> 16);
+    const unsigned long long nxt = (md << 48) | (lo << 8);
+    const int sh = __clzll((long long)t1);
+    unsigned long long qv = t1, lost = nxt;
+    if (sh) { qv = (t1 << sh) | (nxt >> (64 - sh)); lost = nxt << sh; }
+    if (sticky || lost != 0ULL) qv |= 1ULL;
+    const double d = __ull2double_rn(qv);
+    const int e = 40 * ct - 24 - sh + scale_exp;
+    // one multiplication by an exact 2^e rounds d 2^e once, exactly as ldexp does; ldexp covers the rest
+    if (e >= -1022 && e <= 1023) return d * __longlong_as_double((long long)(e + 1023) << 52);
+    return ldexp(d, e);
+}
+
+// chunks of 40 bits of M = m_0 ... m_{N-1} (at least 2), per N
+__host__ __device__ constexpr int chunks_for(int N) {
+    constexpr int c[OZK_NMAX + 1] = {2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 3, 3, 3, 3, 3, 4,
+                                     4, 4, 4, 4, 5, 5, 5, 5, 5, 5, 6, 6, 6, 6, 6, 7};
+    return c[N];
+}
+
+template <int N>
 __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ X, const int32_t* __restrict__ r,
                                                     const int32_t* __restrict__ cexp, const int32_t* __restrict__ p_dev,
                                                     int m, int n, const __grid_constant__ ReconParams rp,
                                                     double* __restrict__ Cout) {
+    constexpr int C = chunks_for(N);
     const long long quads = (long long)m * (n >> 2);
     const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= quads) return;
@@ -97,23 +112,23 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
     const int i = (int)(g / n4), j4 = (int)(g - (long long)i * n4);
     const size_t mn = (size_t)m * n;
     const size_t idx = (size_t)i * n + 4 * (size_t)j4;
+    unsigned w[N];
+#pragma unroll
+    for (int t = 0; t < N; t++) w[t] = __ldg(reinterpret_cast<const unsigned*>(X + (size_t)t * mn + idx));
     double acc[4][C];
 #pragma unroll
     for (int e = 0; e < 4; e++)
 #pragma unroll
         for (int c = 0; c < C; c++) acc[e][c] = 0.0;
-    const int N = rp.N;
 #pragma unroll
-    for (int t = 0; t < OZK_NMAX; t++) {
-        if (t < N) {
-            const unsigned w = __ldg(reinterpret_cast<const unsigned*>(X + (size_t)t * mn + idx));
+    for (int t = 0; t < N; t++) {
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                // exact double of the byte: 2^52 + b, minus 2^52
-                const double xd = __hiloint2double(0x43300000, (int)((w >> (8 * e)) & 0xffu)) - 4503599627370496.0;
+        for (int e = 0; e < 4; e++) {
+            // exact double of the byte: 2^52 + b, minus 2^52
+            const double xd = __hiloint2double(0x43300000, (int)__byte_perm(w[t], 0u, 0x4440u | (unsigned)e)) -
+                              4503599627370496.0;
 #pragma unroll
-                for (int c = 0; c < C; c++) acc[e][c] = fma(xd, rp.V[t][c], acc[e][c]);
-            }
+            for (int c = 0; c < C; c++) acc[e][c] = fma(xd, rp.V[t][c], acc[e][c]);
         }
     }
     const int p = *p_dev;
@@ -132,7 +147,7 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
         // X must lie in [-M/2, M/2 - 1]; outside the bound of pmax_bits only, checked exactly when close
         double approx = 0.0;
 #pragma unroll
-        for (int c = 0; c < C; c++) approx = fma(a[c], ldexp(1.0, 40 * c), approx);
+        for (int c = 0; c < C; c++) approx = fma(a[c], rp.P40[c], approx);
         if (fabs(approx) > 0.4999 * rp.Mf) {
             double tmp[C];
 #pragma unroll
@@ -146,12 +161,12 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
                 if (is_negative<C>(tmp)) sub_scaled<C>(a, rp.Mc, -1.0);
             }
         }
+        // magnitude, without a divergent branch: multiply by the sign and normalise again
         const bool neg = is_negative<C>(a);
-        if (neg) {
+        const double sg = neg ? -1.0 : 1.0;
 #pragma unroll
-            for (int c = 0; c < C; c++) a[c] = -a[c];
-            normalize<C>(a);
-        }
+        for (int c = 0; c < C; c++) a[c] *= sg;
+        normalize<C>(a);
         const double v = to_double_unscaled<C>(a, base + cj[e]);
         outv[e] = neg ? -v : v;
     }
@@ -233,6 +248,7 @@ ReconParams make_params(int N) {
         rp.Mc[c] = big_chunk40(M, c);
         rp.Mh[c] = big_chunk40(Mh, c);
         rp.invM[c] = ldexp(1.0, 40 * c) / rp.Mf;
+        rp.P40[c] = ldexp(1.0, 40 * c);
     }
     return rp;
 }
@@ -260,14 +276,14 @@ extern "C" int ozk_reconstruct(const uint8_t* X, const int32_t* r, const int32_t
     const long long quads = (long long)m * (n >> 2);
     const long long blocks = (quads + 255) / 256;
     if (blocks > 0x7fffffffLL) return OZK_ERR_ARG;
-    switch (rp.C) {
-        case 1:
-        case 2: recon_kernel<2><<<(unsigned)blocks, 256, 0, st>>>(X, r, c, p_dev, m, n, rp, C); break;
-        case 3: recon_kernel<3><<<(unsigned)blocks, 256, 0, st>>>(X, r, c, p_dev, m, n, rp, C); break;
-        case 4: recon_kernel<4><<<(unsigned)blocks, 256, 0, st>>>(X, r, c, p_dev, m, n, rp, C); break;
-        case 5: recon_kernel<5><<<(unsigned)blocks, 256, 0, st>>>(X, r, c, p_dev, m, n, rp, C); break;
-        case 6: recon_kernel<6><<<(unsigned)blocks, 256, 0, st>>>(X, r, c, p_dev, m, n, rp, C); break;
-        default: recon_kernel<7><<<(unsigned)blocks, 256, 0, st>>>(X, r, c, p_dev, m, n, rp, C); break;
+    switch (N) {
+#define OZK_RC(NN) case NN: recon_kernel<NN><<<(unsigned)blocks, 256, 0, st>>>(X, r, c, p_dev, m, n, rp, C); break;
+        OZK_RC(1) OZK_RC(2) OZK_RC(3) OZK_RC(4) OZK_RC(5) OZK_RC(6) OZK_RC(7) OZK_RC(8)
+        OZK_RC(9) OZK_RC(10) OZK_RC(11) OZK_RC(12) OZK_RC(13) OZK_RC(14) OZK_RC(15) OZK_RC(16)
+        OZK_RC(17) OZK_RC(18) OZK_RC(19) OZK_RC(20) OZK_RC(21) OZK_RC(22) OZK_RC(23) OZK_RC(24)
+        OZK_RC(25) OZK_RC(26) OZK_RC(27) OZK_RC(28) OZK_RC(29) OZK_RC(30) OZK_RC(31) OZK_RC(32)
+#undef OZK_RC
+        default: return OZK_ERR_ARG;
     }
     OZK_CHECK_LAUNCH();
     return OZK_OK;

@@ -6,7 +6,8 @@
 //   X = sign(v) x, residue = X mod m_t mapped to the symmetric range [-floor(m_t/2), ceil(m_t/2) - 1] as int8,
 //   with ag = p - r_i + gamma_l for A and ag = p - c_j - gamma_l for B.
 //
-// Method (this build's own): X < 2^(p+1) is cut into 10-bit digits d_q (at most 16 for p <= 159).  For each modulus,
+// Method (this build's own): X < 2^(p+1) is cut into 10-bit digits d_q (at most 16 for p <= 159), computed with
+// exact FP64 operations (make_digits).  For each modulus,
 // s = sum_q d_q (2^(10q) mod m_t) is an integer below 2^22, so the sum, the quotient rint(s / m_t) and the
 // remainder s - m_t rint(s / m_t) are all exact in FP32 (the quotient is exact because s / m_t, m_t odd, stays at
 // least 1/(2 m_t) away from a half-integer while fl(1/m_t) errs by less than that over |s| < 2^22; m_t = 256 is
@@ -42,41 +43,28 @@ __constant__ SplitTables c_split = make_split_tables();
 
 constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23: adding it rounds a |value| < 2^22 to an integer
 
-// 10-bit digits of X = round(|v| 2^ag), negated when v < 0
+// 10-bit digits of X = round(|v| 2^ag) as floats, negated when v < 0, computed with exact FP64 operations:
+// t = |v| 2^ag is a power-of-two scaling (exact; a result below 2^-1022 can only give X = 0),
+// X = floor(t) + [t - floor(t) >= 1/2] rounds half away from zero, F_0 = X, F_{q+1} = floor(F_q / 1024) (exact
+// scalings and floors), and the digit d_q = F_q - 1024 F_{q+1} is exact (Sterbenz).  This keeps the integer
+// pipe free: the whole decomposition runs on the FP64 pipe, the residues on the FP32 pipe.
 template <int ND>
 __device__ __forceinline__ void make_digits(double v, int ag, float (&d)[ND]) {
-    const unsigned long long b = ozk_bits(v);
-    const bool neg = (b >> 63) != 0ULL;
-    const unsigned E = (unsigned)((b >> 52) & 0x7ffu);
-    const unsigned long long f = b & 0xfffffffffffffULL;
-    unsigned long long mant;
-    int e2;
-    if (E == 0u) { mant = f; e2 = -1074; } else { mant = f | (1ULL << 52); e2 = (int)E - 1075; }
-    const int s = e2 + ag;
-    unsigned long long x;
-    int sh;
-    if (mant == 0ULL) { x = 0ULL; sh = 0; }
-    else if (s >= 0) { x = mant; sh = s; }
-    else { const int q = -s; x = (q >= 54) ? 0ULL : ((mant + (1ULL << (q - 1))) >> q); sh = 0; }
-    if (sh > OZK_PMAX_SUPPORTED) { x = 0ULL; sh = 0; }   // out of the supported range: never reached for valid p
-    // X = x << sh as three 64-bit words (sh <= 159, x < 2^54)
-    const int ws = sh >> 6, bs = sh & 63;
-    const unsigned long long lo = x << bs;
-    const unsigned long long hi = bs ? (x >> (64 - bs)) : 0ULL;
-    const unsigned long long w0 = ws == 0 ? lo : 0ULL;
-    const unsigned long long w1 = ws == 0 ? hi : (ws == 1 ? lo : 0ULL);
-    const unsigned long long w2 = ws == 1 ? hi : (ws == 2 ? lo : 0ULL);
+    const double av = fabs(v);
+    const bool neg = (ozk_bits(v) >> 63) != 0ULL;
+    double tv;
+    if (ag >= -1022 && ag <= 1023) tv = av * __longlong_as_double((long long)(ag + 1023) << 52);
+    else tv = ldexp(av, ag);
+    const double fl = floor(tv);
+    double F = fl + ((tv - fl >= 0.5) ? 1.0 : 0.0);   // X
 #pragma unroll
     for (int q = 0; q < ND; q++) {
-        const int off = 10 * q, wi = off >> 6, bo = off & 63;
-        const unsigned long long cur = wi == 0 ? w0 : (wi == 1 ? w1 : w2);
-        unsigned long long val = cur >> bo;
-        if (bo > 54) {
-            const unsigned long long nxt = wi == 0 ? w1 : (wi == 1 ? w2 : 0ULL);
-            val |= nxt << (64 - bo);
-        }
-        const unsigned dq = (unsigned)(val & 1023ULL);
-        const float fd = __fsub_rn(__uint_as_float(0x4B000000u | dq), 8388608.0f);
+        const double Fn = floor(F * 0.0009765625);     // floor(X 2^-10(q+1)) = floor(floor(X 2^-10q) / 1024)
+        const double dq = fma(-1024.0, Fn, F);
+        F = Fn;
+        // the low word of 2^52 + d is d; 2^23 + d as a float is exact, minus 2^23
+        const unsigned di = (unsigned)__double2loint(dq + 4503599627370496.0);
+        const float fd = __fsub_rn(__uint_as_float(0x4B000000u | di), 8388608.0f);
         d[q] = neg ? -fd : fd;
     }
 }
