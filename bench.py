@@ -161,8 +161,8 @@ def cpu_baseline(pkg, A_host, B_host, N, sample, phi):
 
 
 def auto_sample(k, N, threads):
-    # about 10-20 s of CPU work at ~1.5 G int8 MAC/s per thread (scalar-ish int8 dot products)
-    macs = 15.0 * 1.5e9 * max(1, threads)
+    # about 10-15 s of CPU work: the port's int8 products ran at ~7.7 G MAC/s per thread on the GPU boxes' host cores
+    macs = 12.0 * 7.0e9 * max(1, threads)
     s = int((macs / (k * N)) ** 0.5)
     return max(32, min(2048, (s // 32) * 32))
 
@@ -233,12 +233,13 @@ def main():
     C = torch.empty((rows, n), dtype=torch.float64, device=dev)
     t_gen = time.perf_counter() - t_gen
 
+    step_events = []
     if world > 1:
         E = pkg.DistributedOzakiCRT()
-        call = lambda: E.run(A, B, C, force_N=forceN)  # noqa: E731
+        call = lambda ev=None: E.run(A, B, C, force_N=forceN)  # noqa: E731
     else:
         E = pkg.OzakiCRT()
-        call = lambda: E.run(A, B, C, graph=True, force_N=forceN)  # noqa: E731
+        call = lambda ev=None: E.run_fast(A, B, C, force_N=forceN, events=ev)  # noqa: E731
 
     for _ in range(args.warmup):
         _, info = call()
@@ -256,7 +257,10 @@ def main():
             dist.barrier()
         e0.record(stream)
         for _ in range(args.steps):
-            _, info = call()
+            ev = [] if world == 1 else None
+            _, info = call(ev)
+            if ev:
+                step_events.append(ev)
         e1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -269,6 +273,12 @@ def main():
         t_dev = float(tt.item())
     flops = 2.0 * m * n * k
     value = flops / t_dev / 1e12
+
+    # stage times inside the timed calls (CUDA events between the parts of run_fast)
+    in_step = {}
+    for ev in step_events:
+        for (n0, a), (n1, b_) in zip(ev[:-1], ev[1:]):
+            in_step[n1] = in_step.get(n1, 0.0) + a.elapsed_time(b_) / len(step_events)
 
     # roofline of the dominant kernel (the INT8 products with the fused reduction): live CUDA-event time per launch
     Nplanes = info.get("N") or forceN
@@ -287,7 +297,7 @@ def main():
                 "peak_source": "cuBLASLt INT8 GEMM 8192^3 burst measured in this run (torch._int_mm)",
                 "bf16_measured_tflops_x2": 2 * bf16_peak, "frac_of_2x_bf16": achieved / (2 * bf16_peak),
                 "traffic": None, "algorithmic_ops_per_launch": int8_ops, "ms_per_launch": t_gemm * 1e3,
-                "stages_ms": {k_: v * 1e3 / 3 for k_, v in prof.items()}}
+                "stages_ms": {k_: v * 1e3 / 3 for k_, v in prof.items()}, "timed_call_stages_ms": in_step}
 
     # accuracy on a sample (rank 0's block): E1 / E2 against the correctly rounded product, native DGEMM beside it
     acc = None

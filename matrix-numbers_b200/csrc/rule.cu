@@ -76,16 +76,15 @@ __device__ __forceinline__ bool before(double v, int i, double bv, int bi) {
     return v > bv || (v == bv && i < bi);
 }
 
-// Select the `cnt` first indices of the stable descending order of hard values; writes them to out[0..cnt).
-__device__ void top_hard(const int32_t* __restrict__ e, const double* __restrict__ s, int len, int k, int cnt, int* out,
-                         double* smv, int* smi) {
+// Select the `cnt` first indices of the stable descending order of the values hv[0..len); writes them to out[0..cnt).
+__device__ void top_hard(const double* __restrict__ hv, int len, int cnt, int* out, double* smv, int* smi) {
     double pv = INFINITY;
     int pi = -1;
     for (int round = 0; round < cnt; round++) {
         double bv = -INFINITY;
         int bi = 0x7fffffff;
         for (int x = threadIdx.x; x < len; x += blockDim.x) {
-            const double v = hard_value(e[x], s[x], k);
+            const double v = hv[x];
             const bool after_prev = (v < pv) || (v == pv && x > pi);
             if (after_prev && before(v, x, bv, bi)) { bv = v; bi = x; }
         }
@@ -139,7 +138,7 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
     const double* __restrict__ nA, const double* __restrict__ sB, const double* __restrict__ nB,
     const int32_t* __restrict__ flag, const int64_t* __restrict__ Ir, int nIr, const int64_t* __restrict__ Jr, int nJr,
     int m, int n, int k, int force_N, int force_p, MTable mt, RuleCtl* __restrict__ ctl, int32_t* __restrict__ dec,
-    int32_t* __restrict__ p_dev, double* __restrict__ aux) {
+    int32_t* __restrict__ p_dev, double* __restrict__ aux, double* __restrict__ hv) {
     __shared__ double smv[32];
     __shared__ int smi[32];
     // max nA, max nB (order-independent)
@@ -176,8 +175,12 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
     // caller-supplied probe indices are clamped into range (an out-of-range index must not be dereferenced)
     for (int x = threadIdx.x; x < nIr; x += blockDim.x) ctl->I[x] = (Ir[x] >= 0 && Ir[x] < m) ? (int)Ir[x] : 0;
     for (int x = threadIdx.x; x < nJr; x += blockDim.x) ctl->J[x] = (Jr[x] >= 0 && Jr[x] < n) ? (int)Jr[x] : 0;
-    top_hard(r, sA, m, k, hr, ctl->I + nIr, smv, smi);
-    top_hard(c, sB, n, k, hc, ctl->J + nJr, smv, smi);
+    // the hard values 2^e k / s, computed once into the workspace, then the stable top-32 of rows and of columns
+    for (int x = threadIdx.x; x < m; x += blockDim.x) hv[x] = hard_value(r[x], sA[x], k);
+    for (int x = threadIdx.x; x < n; x += blockDim.x) hv[m + x] = hard_value(c[x], sB[x], k);
+    __syncthreads();
+    top_hard(hv, m, hr, ctl->I + nIr, smv, smi);
+    top_hard(hv + m, n, hc, ctl->J + nJr, smv, smi);
 }
 
 // split-K probe product: partial[b][a][j] = sum over this block's contraction tiles of |A_I[a] l| |B_l J[j]|
@@ -351,17 +354,18 @@ int probe_blocks(int k) {
 }
 
 size_t ctl_bytes() { return (sizeof(RuleCtl) + 255) & ~(size_t)255; }
+size_t hard_bytes(int m, int n) { return ((size_t)(m + n) * sizeof(double) + 255) & ~(size_t)255; }
 
 }  // namespace
 
 extern "C" size_t ozk_rule_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
-    return ctl_bytes() + (size_t)(probe_blocks(k) + 1) * kProbeMax * kProbeMax * sizeof(double);
+    return ctl_bytes() + hard_bytes(m, n) + (size_t)(probe_blocks(k) + 1) * kProbeMax * kProbeMax * sizeof(double);
 }
 
 extern "C" size_t ozk_rule_probe_offset(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
-    return ctl_bytes() + (size_t)probe_blocks(k) * kProbeMax * kProbeMax * sizeof(double);
+    return ctl_bytes() + hard_bytes(m, n) + (size_t)probe_blocks(k) * kProbeMax * kProbeMax * sizeof(double);
 }
 
 extern "C" int ozk_rule_prepare(const int32_t* r, const int32_t* c, const double* sA, const double* nA, const double* sB,
@@ -381,9 +385,10 @@ extern "C" int ozk_rule_prepare(const int32_t* r, const int32_t* c, const double
     MTable mt;
     for (int N = 0; N <= OZK_NMAX; N++) mt.M[N] = N ? ozk_modulus_product(N) : 1.0;
     RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
+    double* hv = reinterpret_cast<double*>(static_cast<char*>(workspace) + ctl_bytes());
     rule_prep_kernel<<<1, kPrepThreads, 0, st>>>(r, c, sA, nA, sB, nB, flag, probe_rows, n_probe_rows, probe_cols,
                                                  n_probe_cols, m, n, k, force_N, force_N > 0 ? force_p : -1, mt, ctl, dec,
-                                                 p_dev, aux);
+                                                 p_dev, aux, hv);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }
@@ -395,7 +400,7 @@ extern "C" int ozk_rule_probe(const double* A_rows, const double* B, int row_beg
     if (workspace_bytes < ozk_rule_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
     RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
-    double* partial = reinterpret_cast<double*>(static_cast<char*>(workspace) + ctl_bytes());
+    double* partial = reinterpret_cast<double*>(static_cast<char*>(workspace) + ctl_bytes() + hard_bytes(m, n));
     const int nb = probe_blocks(k);
     probe_partial_kernel<<<nb, kProbeThreads, 0, st>>>(A_rows, B, row_begin, rows, n, k, ctl, partial);
     OZK_CHECK_LAUNCH();

@@ -95,8 +95,34 @@ __global__ void gamma_kernel(const unsigned long long* __restrict__ colmax, cons
     gam[l] = (!enable || bad || ea == OZK_NEG || eb == OZK_NEG) ? 0 : ((eb - ea) >> 1);
 }
 
+// x 2^e for |e| in the normal exponent range by one multiplication with an exact power of two (exact unless the
+// result leaves the normal range, where ldexp takes over)
+__device__ __forceinline__ double scale2(double x, int e) {
+    if (e >= -1022 && e <= 1023) return x * __longlong_as_double((long long)(e + 1023) << 52);
+    return ldexp(x, e);
+}
+
+// Running statistics of a set of values |x| 2^g (x != 0) with a running maximum exponent emax:
+//   s = sum |x| 2^g,  q = sum (|x| 2^(g - emax))^2.
+// When emax grows by d, q is rescaled by 2^-2d (an exact power-of-two scaling), so one pass gives the same sums as the
+// reference's two passes (max first, then sums relative to it) up to the order of additions.
+struct RunStats {
+    int emax;
+    double s, q;
+    __device__ __forceinline__ void init() { emax = OZK_NEG; s = 0.0; q = 0.0; }
+    __device__ __forceinline__ void add(double x, int e_plus_g, int g) {   // x = |value| != 0
+        if (e_plus_g > emax) {
+            if (emax != OZK_NEG) q = scale2(q, -2 * (e_plus_g - emax));
+            emax = e_plus_g;
+        }
+        s += scale2(x, g);
+        const double y = scale2(x, g - emax);
+        q = fma(y, y, q);
+    }
+};
+
 // r_i = max_l (e(A_il) + gamma_l) over non-zeros (0 if none); sA_i = sum |A_il| 2^gamma_l;
-// nA_i = sum (|A_il| 2^(gamma_l - r_i))^2   (rowstatsA_k, :904-925); one block per row
+// nA_i = sum (|A_il| 2^(gamma_l - r_i))^2   (rowstatsA_k, :904-925); one block per row, one pass over the row
 __global__ void __launch_bounds__(kThreads) rowstats_a_kernel(const double* __restrict__ A, const int32_t* __restrict__ gam, int k,
                                                               int32_t* __restrict__ r_out, double* __restrict__ s_out,
                                                               double* __restrict__ n_out) {
@@ -105,85 +131,65 @@ __global__ void __launch_bounds__(kThreads) rowstats_a_kernel(const double* __re
     const int i = blockIdx.x;
     const double2* row = reinterpret_cast<const double2*>(A + (size_t)i * k);
     const int2* g2 = reinterpret_cast<const int2*>(gam);
-    int mx = OZK_NEG;
+    RunStats rs;
+    rs.init();
     for (int h = threadIdx.x; h < k / 2; h += kThreads) {
         const double2 v = __ldg(row + h);
         const int2 g = __ldg(g2 + h);
-        int e0 = ozk_fexp(ozk_bits(v.x) & OZK_ABSMASK), e1 = ozk_fexp(ozk_bits(v.y) & OZK_ABSMASK);
-        if (e0 != OZK_NEG) mx = max(mx, e0 + g.x);
-        if (e1 != OZK_NEG) mx = max(mx, e1 + g.y);
+        const int e0 = ozk_fexp(ozk_bits(v.x) & OZK_ABSMASK), e1 = ozk_fexp(ozk_bits(v.y) & OZK_ABSMASK);
+        if (e0 != OZK_NEG) rs.add(fabs(v.x), e0 + g.x, g.x);
+        if (e1 != OZK_NEG) rs.add(fabs(v.y), e1 + g.y, g.y);
     }
-    int rr = block_reduce(mx, (int)OZK_NEG, smi, MaxI());
-    if (rr <= OZK_NEG / 2) rr = 0;
-    double s = 0.0, q = 0.0;
-    for (int h = threadIdx.x; h < k / 2; h += kThreads) {
-        const double2 v = __ldg(row + h);
-        const int2 g = __ldg(g2 + h);
-        const double x0 = fabs(v.x), x1 = fabs(v.y);
-        if (x0 != 0.0) { s += ldexp(x0, g.x); const double y = ldexp(x0, g.x - rr); q += y * y; }
-        if (x1 != 0.0) { s += ldexp(x1, g.y); const double y = ldexp(x1, g.y - rr); q += y * y; }
-    }
-    s = block_sum(s, smd);
-    q = block_sum(q, smd);
-    if (threadIdx.x == 0) { r_out[i] = rr; s_out[i] = s; n_out[i] = q; }
+    const int mx = block_reduce(rs.emax, (int)OZK_NEG, smi, MaxI());
+    const int rr = mx <= OZK_NEG / 2 ? 0 : mx;
+    const double q = rs.emax == OZK_NEG ? 0.0 : scale2(rs.q, -2 * (mx - rs.emax));
+    const double s = block_sum(rs.s, smd);
+    const double qq = block_sum(q, smd);
+    if (threadIdx.x == 0) { r_out[i] = rr; s_out[i] = s; n_out[i] = qq; }
 }
 
-__global__ void fill_i32_kernel(int32_t* __restrict__ p, int count, int v) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < count) p[i] = v;
-}
-
-// c_j = max_l (e(B_lj) - gamma_l) over non-zeros (colexpB_k, :926-937): 2 columns per thread, kColChunk rows
-__global__ void __launch_bounds__(kThreads) colexp_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ gam, int k,
-                                                            int n, int32_t* __restrict__ c_out) {
+// column statistics of B over one chunk of kColChunk rows, 2 columns per thread, one pass (colexpB_k and colsumsB_k,
+// :926-951): per chunk the local maximum exponent, sB partial and nB partial relative to the local maximum
+__global__ void __launch_bounds__(kThreads) colstats_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ gam,
+                                                              int k, int n, int32_t* __restrict__ pc,
+                                                              double* __restrict__ ps, double* __restrict__ pq) {
     const int j = 2 * (blockIdx.x * kThreads + threadIdx.x);
     if (j >= n) return;
     const int l0 = blockIdx.y * kColChunk, l1 = min(k, l0 + kColChunk);
-    int m0 = OZK_NEG, m1 = OZK_NEG;
-    for (int l = l0; l < l1; l++) {
-        const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2*>(B + (size_t)l * n + j));
-        const int g = __ldg(gam + l);
-        const int e0 = ozk_fexp(v.x & OZK_ABSMASK), e1 = ozk_fexp(v.y & OZK_ABSMASK);
-        if (e0 != OZK_NEG) m0 = max(m0, e0 - g);
-        if (e1 != OZK_NEG) m1 = max(m1, e1 - g);
-    }
-    if (m0 > OZK_NEG / 2) atomicMax(c_out + j, m0);
-    if (m1 > OZK_NEG / 2) atomicMax(c_out + j + 1, m1);
-}
-
-// partial sB / nB over one chunk of rows (colsumsB_k, :938-951), written per chunk instead of atomically added
-__global__ void __launch_bounds__(kThreads) colsums_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ gam,
-                                                             const int32_t* __restrict__ c, int k, int n,
-                                                             double* __restrict__ ps, double* __restrict__ pq) {
-    const int j = 2 * (blockIdx.x * kThreads + threadIdx.x);
-    if (j >= n) return;
-    int c0 = c[j], c1 = c[j + 1];
-    if (c0 <= OZK_NEG / 2) c0 = 0;
-    if (c1 <= OZK_NEG / 2) c1 = 0;
-    const int l0 = blockIdx.y * kColChunk, l1 = min(k, l0 + kColChunk);
-    double s0 = 0.0, s1 = 0.0, q0 = 0.0, q1 = 0.0;
+    RunStats r0, r1;
+    r0.init();
+    r1.init();
     for (int l = l0; l < l1; l++) {
         const double2 v = __ldg(reinterpret_cast<const double2*>(B + (size_t)l * n + j));
-        const int g = __ldg(gam + l);
-        const double x0 = fabs(v.x), x1 = fabs(v.y);
-        if (x0 != 0.0) { s0 += ldexp(x0, -g); const double y = ldexp(x0, -g - c0); q0 += y * y; }
-        if (x1 != 0.0) { s1 += ldexp(x1, -g); const double y = ldexp(x1, -g - c1); q1 += y * y; }
+        const int g = -__ldg(gam + l);
+        const int e0 = ozk_fexp(ozk_bits(v.x) & OZK_ABSMASK), e1 = ozk_fexp(ozk_bits(v.y) & OZK_ABSMASK);
+        if (e0 != OZK_NEG) r0.add(fabs(v.x), e0 + g, g);
+        if (e1 != OZK_NEG) r1.add(fabs(v.y), e1 + g, g);
     }
     const size_t o = (size_t)blockIdx.y * n + j;
-    ps[o] = s0; ps[o + 1] = s1;
-    pq[o] = q0; pq[o + 1] = q1;
+    pc[o] = r0.emax; pc[o + 1] = r1.emax;
+    ps[o] = r0.s; ps[o + 1] = r1.s;
+    pq[o] = r0.q; pq[o + 1] = r1.q;
 }
 
-// chunk partials summed in chunk order; c normalised (no non-zero -> 0, as its consumers do at :1257, :1060)
-__global__ void colsums_final_kernel(const double* __restrict__ ps, const double* __restrict__ pq, int nchunks, int n,
-                                     int32_t* __restrict__ c, double* __restrict__ sB, double* __restrict__ nB) {
+// chunk partials combined in chunk order: c_j = max of the local maxima (0 when the column has no non-zero, as the
+// consumers of c do at :1257, :1060), sB_j = sum, nB_j = sum of the partials rescaled to c_j
+__global__ void colstats_final_kernel(const int32_t* __restrict__ pc, const double* __restrict__ ps,
+                                      const double* __restrict__ pq, int nchunks, int n, int32_t* __restrict__ c,
+                                      double* __restrict__ sB, double* __restrict__ nB) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= n) return;
+    int mx = OZK_NEG;
+    for (int h = 0; h < nchunks; h++) mx = max(mx, pc[(size_t)h * n + j]);
     double s = 0.0, q = 0.0;
-    for (int h = 0; h < nchunks; h++) { s += ps[(size_t)h * n + j]; q += pq[(size_t)h * n + j]; }
+    for (int h = 0; h < nchunks; h++) {
+        const int e = pc[(size_t)h * n + j];
+        s += ps[(size_t)h * n + j];
+        if (e != OZK_NEG) q += scale2(pq[(size_t)h * n + j], -2 * (mx - e));
+    }
     sB[j] = s;
     nB[j] = q;
-    if (c[j] <= OZK_NEG / 2) c[j] = 0;
+    c[j] = mx <= OZK_NEG / 2 ? 0 : mx;
 }
 
 }  // namespace
@@ -193,7 +199,7 @@ static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 extern "C" size_t ozk_stats_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
     const size_t nchunks = ((size_t)k + kColChunk - 1) / kColChunk;
-    return align256((size_t)k * 8) * 2 + align256(nchunks * (size_t)n * 8) * 2;
+    return align256((size_t)k * 8) * 2 + align256(nchunks * (size_t)n * 8) * 2 + align256(nchunks * (size_t)n * 4);
 }
 
 extern "C" int ozk_stats_colmax(const double* A, int m, int k, uint64_t* colmax, ozk_stream_t stream_) {
@@ -229,14 +235,11 @@ extern "C" int ozk_stats_finish(const double* A, const double* B, int m, int n, 
     OZK_CHECK_LAUNCH();
     rowstats_a_kernel<<<m, kThreads, 0, st>>>(A, gam, k, r, sA, nA);
     OZK_CHECK_LAUNCH();
-    fill_i32_kernel<<<(n + 255) / 256, 256, 0, st>>>(c, n, OZK_NEG);
-    OZK_CHECK_LAUNCH();
+    int32_t* pc = reinterpret_cast<int32_t*>(ws + 2 * align256((size_t)k * 8) + 2 * align256((size_t)nchunks * n * 8));
     const dim3 g2((n / 2 + kThreads - 1) / kThreads, nchunks);
-    colexp_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, c);
+    colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, pc, ps, pq);
     OZK_CHECK_LAUNCH();
-    colsums_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, c, k, n, ps, pq);
-    OZK_CHECK_LAUNCH();
-    colsums_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(ps, pq, nchunks, n, c, sB, nB);
+    colstats_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }

@@ -62,7 +62,7 @@ class CudaOps:
                                         ptr(b["r"]), ptr(b["c"]), ptr(b["sA"]), ptr(b["nA"]), ptr(b["sB"]), ptr(b["nB"]),
                                         ptr(b["flag"]), ptr(b["ws_stats"]), b["ws_stats"].numel(), self._stream()),
               "ozk_stats_finish")
-        self.engine.launches += 7
+        self.engine.launches += 5
         return {"gam": b["gam"], "r": b["r"], "sA": b["sA"], "nA": b["nA"], "c": b["c"], "sB": b["sB"], "nB": b["nB"],
                 "flag": b["flag"], "_b": b}
 

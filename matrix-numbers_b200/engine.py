@@ -128,7 +128,7 @@ class OzakiCRT:
                                 ptr(b["sA"]), ptr(b["nA"]), ptr(b["sB"]), ptr(b["nB"]), ptr(b["flag"]),
                                 ptr(b["ws_stats"]), b["ws_stats"].numel(), st)
         check(rc, "ozk_stats")
-        self.launches += 8
+        self.launches += 6
 
     # ---- stage 2: the a-priori rule on the device ---------------------------------------------------------------
     def _rule_device(self, A, B, b, tau, safety, force_N=None, force_p=None, seed=0, stream=None):
@@ -252,8 +252,9 @@ class OzakiCRT:
         g.replay()
         self.launches += 4
 
-    def run_fast(self, A, B, C, tau=2.0 ** -52, safety=2.0, inside=True, force_N=None, force_p=None):
-        """Timed path: [graph: statistics + rule] -> one host read of (N, p) -> [graph: residues, products, recon]."""
+    def run_fast(self, A, B, C, tau=2.0 ** -52, safety=2.0, inside=True, force_N=None, force_p=None, events=None):
+        """Timed path: [graph: statistics + rule] -> one host read of (N, p) -> [graph: residues, products, recon].
+        ``events`` (a list) receives (name, CUDA event) marks after each part, for stage timing inside a run."""
         self._shape_check(A, B, C)
         m, k = A.shape
         n = B.shape[1]
@@ -263,9 +264,18 @@ class OzakiCRT:
         if g is None:
             g = self._capture(lambda: self._stats_rule(A, B, b, tau, safety, inside, force_N, force_p))
             self.graphs[key] = g
+
+        def mark(name):
+            if events is not None:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                events.append((name, e))
+        mark("start")
         g.replay()
-        self.launches += 12
+        mark("stats+rule")
+        self.launches += 10
         ctl, _ = self._read_ctl(b)
+        mark("host read")
         N, p, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
         if fb or N == 0:
             torch.matmul(A, B, out=C)
@@ -278,6 +288,7 @@ class OzakiCRT:
             ctl, _ = self._read_ctl(b)
             N, p = ctl[0], ctl[1]
         self.core_graph(A, B, b, N, C)
+        mark("core")
         return C, {"N": N, "p": p, "preq": preq}
 
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, graph=False, prof=None, seed=0, config=None,
