@@ -1,39 +1,52 @@
-// Stage 3a: residue split.  FP64 A and B are read once (16-byte and 8-byte coalesced loads) and all N symmetric
-// INT8 residue planes are written in the same pass, both K-major (the operand layout of the tcgen05 GEMM).
+// Stage 3a: residue split.  FP64 A and B are read once and all N symmetric INT8 residue planes are written in the
+// same pass, both K-major (the operand layout of the tcgen05 GEMM).
 //
 // Semantics (the reference's decomp / resid / resA_k / resB_k, code/ozaki_engine.py:971-1038):
 //   x = round(|v| 2^ag) (exact when the shift is to the left, round half away from zero otherwise),
 //   X = sign(v) x, residue = X mod m_t mapped to the symmetric range [-floor(m_t/2), ceil(m_t/2) - 1] as int8,
 //   with ag = p - r_i + gamma_l for A and ag = p - c_j - gamma_l for B.
 //
-// Method (this build's own): X < 2^(p+1) is cut into 10-bit digits d_q (at most 16 for p <= 159), computed with
-// exact FP64 operations (make_digits).  For each modulus,
-// s = sum_q d_q (2^(10q) mod m_t) is an integer below 2^22, so the sum, the quotient rint(s / m_t) and the
-// remainder s - m_t rint(s / m_t) are all exact in FP32 (the quotient is exact because s / m_t, m_t odd, stays at
-// least 1/(2 m_t) away from a half-integer while fl(1/m_t) errs by less than that over |s| < 2^22; m_t = 256 is
-// exact).  The remainder is already the symmetric residue; its low byte is read from the float's bits after adding
-// 1.5 * 2^23.  The sign is folded into the digits.  This replaces the reference's integer % chains (mod53, table
-// products) with FP32 fused multiply-adds.
+// Method (this build's own).  Each element becomes a little-endian byte string of KB bytes (KB = 16 for p <= 119,
+// 32 for p <= 159): bytes 0 .. KB-2 hold |X| (<= 2^p), one's-complemented when v < 0, and byte KB-1 is a sign flag.
+// With weights w_q = 2^(8q) mod m_t for the value bytes and w_(KB-1) = (1 - 2^(8(KB-1))) mod m_t for the flag,
+// s_t = sum_q b_q w_q is congruent to X modulo m_t (2^(8(KB-1)) - 1 - |X| + 1 - 2^(8(KB-1)) = -|X| for negative v)
+// and lies in [0, 2^21]:
+// for a warp chunk of 32 elements the sums of all moduli are one small integer matrix product,
+// [16 moduli x KB bytes] x [KB bytes x 32 elements], run as mma.m16n8k16 / m16n8k32 (u8 x u8 -> s32, exact) on the
+// byte strings staged in shared memory and loaded with ldmatrix.  The MMA runs twice, accumulating onto h_t
+// (m_t / 2 for m_t = 256, (m_t - 1) / 2 for odd m_t) and onto 0: q = floor((s + h) / m_t) is one multiply-high by
+// ceil(2^32 / m_t) (exact for s + h < 2^24), and the low byte of s - m_t q is the symmetric residue -- two integer
+// instructions per residue, no per-modulus digit sums and no sign handling.  The element -> MMA column assignment
+// gives each thread 8 consecutive elements of a modulus: one 8-byte store.
 #include "ozk_common.cuh"
 
 namespace {
 
 struct SplitTables {
-    float P[OZK_NMAX];          // m_t
-    float inv[OZK_NMAX];        // fl(1 / m_t)
-    float W[OZK_NMAX][16];      // 2^(10 q) mod m_t
+    unsigned W16[OZK_NMAX][4];   // KB = 16: weight bytes packed 4 per word (little-endian)
+    unsigned W32[OZK_NMAX][8];   // KB = 32
+    unsigned M[OZK_NMAX];        // ceil(2^32 / m_t)
+    int P[OZK_NMAX];
 };
+
+constexpr int pow2_mod(int e, int P) {
+    int w = 1 % P;
+    for (int i = 0; i < e; i++) w = (w * 2) % P;
+    return w;
+}
 
 constexpr SplitTables make_split_tables() {
     SplitTables t{};
     for (int i = 0; i < OZK_NMAX; i++) {
         const int P = ozk_mod(i);
-        t.P[i] = (float)P;
-        t.inv[i] = 1.0f / (float)P;
-        int w = 1 % P;
-        for (int q = 0; q < 16; q++) {
-            t.W[i][q] = (float)w;
-            w = (int)(((long long)w * 1024) % P);
+        t.P[i] = P;
+        t.M[i] = (unsigned)((0x100000000ULL + (unsigned long long)P - 1ULL) / (unsigned long long)P);
+        for (int kb = 16; kb <= 32; kb += 16) {
+            for (int q = 0; q < kb; q++) {
+                const int w = q < kb - 1 ? pow2_mod(8 * q, P) : (1 + P - pow2_mod(8 * (kb - 1), P)) % P;
+                if (kb == 16) t.W16[i][q >> 2] |= (unsigned)w << (8 * (q & 3));
+                else t.W32[i][q >> 2] |= (unsigned)w << (8 * (q & 3));
+            }
         }
     }
     return t;
@@ -41,128 +54,292 @@ constexpr SplitTables make_split_tables() {
 
 __constant__ SplitTables c_split = make_split_tables();
 
-constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23: adding it rounds a |value| < 2^22 to an integer
+#ifndef OZK_SPLIT_MINB
+#define OZK_SPLIT_MINB 2   // resident blocks per SM the register budget is sized for
+#endif
+#ifndef OZK_SPLIT_TC16
+#define OZK_SPLIT_TC16 8   // chunks per warp task for 16-byte strings
+#endif
 
-// 10-bit digits of X = round(|v| 2^ag) as floats, negated when v < 0, computed with exact FP64 operations:
-// t = |v| 2^ag is a power-of-two scaling (exact; a result below 2^-1022 can only give X = 0),
-// X = floor(t) + [t - floor(t) >= 1/2] rounds half away from zero, F_0 = X, F_{q+1} = floor(F_q / 1024) (exact
-// scalings and floors), and the digit d_q = F_q - 1024 F_{q+1} is exact (Sterbenz).  This keeps the integer
-// pipe free: the whole decomposition runs on the FP64 pipe, the residues on the FP32 pipe.
-template <int ND>
-__device__ __forceinline__ void make_digits(double v, int ag, float (&d)[ND]) {
-    const double av = fabs(v);
-    const bool neg = (ozk_bits(v) >> 63) != 0ULL;
-    double tv;
-    if (ag >= -1022 && ag <= 1023) tv = av * __longlong_as_double((long long)(ag + 1023) << 52);
-    else tv = ldexp(av, ag);
-    const double fl = floor(tv);
-    double F = fl + ((tv - fl >= 0.5) ? 1.0 : 0.0);   // X
-#pragma unroll
-    for (int q = 0; q < ND; q++) {
-        const double Fn = floor(F * 0.0009765625);     // floor(X 2^-10(q+1)) = floor(floor(X 2^-10q) / 1024)
-        const double dq = fma(-1024.0, Fn, F);
-        F = Fn;
-        // the low word of 2^52 + d is d; 2^23 + d as a float is exact, minus 2^23
-        const unsigned di = (unsigned)__double2loint(dq + 4503599627370496.0);
-        const float fd = __fsub_rn(__uint_as_float(0x4B000000u | di), 8388608.0f);
-        d[q] = neg ? -fd : fd;
-    }
+constexpr int kWarps = 8;                            // warps per block
+constexpr int kRowBytes = 16;                        // one ldmatrix row: 16 bytes of an element's byte string
+constexpr int kHalfBytes = 32 * kRowBytes;           // one 16-byte half of the strings of a 32-element chunk
+constexpr int kWarpSmem = 8 * (kHalfBytes + 16);     // 8 chunks of KB = 16 (or 4 of KB = 32) per warp, padded
+
+// 64-bit shifts with PTX semantics: amounts at or above 64 (including "negative" ones, as unsigned) give 0
+__device__ __forceinline__ unsigned long long shl64(unsigned long long x, unsigned n) {
+    unsigned long long r;
+    asm("shl.b64 %0, %1, %2;" : "=l"(r) : "l"(x), "r"(n));
+    return r;
+}
+__device__ __forceinline__ unsigned long long shr64(unsigned long long x, unsigned n) {
+    unsigned long long r;
+    asm("shr.b64 %0, %1, %2;" : "=l"(r) : "l"(x), "r"(n));
+    return r;
 }
 
-// symmetric residue byte of the digit vector modulo m_t
-template <int ND>
-__device__ __forceinline__ unsigned residue_bits(const float (&d)[ND], int t) {
-    float s = 0.0f;
+// Byte string of one element as KW 32-bit words (KW = KB / 4).  |v| 2^ag = mant 2^s; X = mant << s for s >= 0,
+// round half up of mant 2^s otherwise (x < 2^54 either way), placed as 64-bit limbs
+// floor(X / 2^(64 j)) mod 2^64 = (x << (sh - 64 j)) | (x >> (64 j - sh)) with clamped shifts.  A negative v takes
+// the one's complement of the value bytes and sets the flag byte; with the flag weight (1 - 2^(8(KB-1))) mod m the
+// string is then congruent to -X (for X = 0 too).
+template <int KW>
+__device__ __forceinline__ void element_words(double v, int ag, unsigned (&w)[KW]) {
+    const unsigned hi = (unsigned)__double2hiint(v), lo = (unsigned)__double2loint(v);
+    const unsigned E = (hi >> 20) & 0x7FFu;
+    const unsigned long long mant = ((unsigned long long)((hi & 0xFFFFFu) | (E ? 0x100000u : 0u)) << 32) | lo;
+    const int s = (int)(E ? E : 1u) - 1075 + ag;
+    const unsigned long long xr = (shr64(mant, (unsigned)(-s - 1)) + 1ULL) >> 1;   // s < 0
+    const unsigned long long x = s < 0 ? xr : mant;
+    const int sh = s < 0 ? 0 : s;
 #pragma unroll
-    for (int q = 0; q < ND; q++) s = __fmaf_rn(d[q], c_split.W[t][q], s);
-    const float qt = __fadd_rn(__fmaf_rn(s, c_split.inv[t], kMagic), -kMagic);
-    const float r = __fmaf_rn(-qt, c_split.P[t], s);
-    return __float_as_uint(__fadd_rn(r, kMagic));   // low byte = r mod 256
+    for (int j = 0; j < KW / 2; j++) {
+        const unsigned long long limb = shl64(x, (unsigned)(sh - 64 * j)) | shr64(x, (unsigned)(64 * j - sh));
+        w[2 * j] = (unsigned)limb;
+        w[2 * j + 1] = (unsigned)(limb >> 32);
+    }
+    const unsigned msk = (unsigned)((int)hi >> 31);
+#pragma unroll
+    for (int i = 0; i < KW; i++) w[i] ^= msk;
+    w[KW - 1] = (w[KW - 1] & 0x00FFFFFFu) | ((hi >> 7) & 0x01000000u);
+}
+
+// Shared-memory row of element e (0..31) of a chunk: ldmatrix matrix j (n-tile j) reads rows 8j .. 8j+7, and row
+// 8j + (c ^ 2j) holds element 8(c >> 1) + 2j + (c & 1), so that the MMA column pairs (2 tig, 2 tig + 1) of the four
+// n-tiles are elements 8 tig .. 8 tig + 7.  The XOR keeps both the row writes of 8 consecutive elements and the 8
+// rows of an ldmatrix matrix on distinct 16-byte bank groups.
+__device__ __forceinline__ int row_of_element(int e) {
+    const int j = (e >> 1) & 3;
+    return 8 * j + (((e & 1) + 2 * (e >> 3)) ^ (2 * j));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, unsigned (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mma_k16(int (&d)[4], const unsigned* a, unsigned b0, int cA, int cB) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.u8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%7, %8, %9, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(b0), "r"(cA), "r"(cA), "r"(cB), "r"(cB));
+}
+
+__device__ __forceinline__ void mma_k32(int (&d)[4], const unsigned* a, unsigned b0, unsigned b1, int cA, int cB) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %11, %12, %13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(cA), "r"(cA), "r"(cB), "r"(cB));
 }
 
 __device__ __forceinline__ unsigned pack4(unsigned b0, unsigned b1, unsigned b2, unsigned b3) {
     return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
 }
 
-// residues of 4 values, all moduli t < N, handed to `emit(t, packed_word)`
-template <int ND, typename Emit>
-__device__ __forceinline__ void quad_residues(const double (&v)[4], const int (&ag)[4], int N, Emit emit) {
-    float d0[ND], d1[ND], d2[ND], d3[ND];
-    make_digits<ND>(v[0], ag[0], d0);
-    make_digits<ND>(v[1], ag[1], d1);
-    make_digits<ND>(v[2], ag[2], d2);
-    make_digits<ND>(v[3], ag[3], d3);
+// Per-lane constants of one 16-modulus row tile (moduli t0 + g and t0 + g + 8 of lane (g, tig)).  The lane-dependent
+// indices into constant memory are read once per thread.
+template <int KB>
+struct TileConsts {
+    unsigned a[KB / 8];   // A fragment: {row g, row g+8} of bytes 4 tig .. 4 tig + 3 (k32: and 16 + 4 tig ..)
+    unsigned MA, MB, nPA, nPB;
+    __device__ __forceinline__ void init(int t0) {
+        const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+        const int tA = t0 + g, tB = t0 + g + 8;   // < 32 = OZK_NMAX
+        if (KB == 16) {
+            a[0] = c_split.W16[tA][tig];
+            a[1] = c_split.W16[tB][tig];
+        } else {
+            a[0] = c_split.W32[tA][tig];
+            a[1] = c_split.W32[tB][tig];
+            a[2] = c_split.W32[tA][4 + tig];
+            a[3] = c_split.W32[tB][4 + tig];
+        }
+        MA = c_split.M[tA];
+        MB = c_split.M[tB];
+        nPA = 0u - (unsigned)c_split.P[tA];
+        nPB = 0u - (unsigned)c_split.P[tB];
+    }
+};
+
+// low byte of s - m floor((s + h) / m), from sh = s + h and s
+__device__ __forceinline__ unsigned residue_byte(int sh, int s, unsigned M, unsigned nP) {
+    return __umulhi((unsigned)sh, M) * nP + (unsigned)s;
+}
+
+// B fragments of a chunk (32 elements, byte strings at shared address `chunk`): four n-tiles, k 0-15 (and 16-31)
+template <int KB>
+__device__ __forceinline__ void chunk_fragments(uint32_t chunk, unsigned (&b)[KB / 4]) {
+    const int lane = threadIdx.x & 31;
+    const int j = lane >> 3, c = lane & 7;
+    const uint32_t addr = chunk + (uint32_t)((8 * j + (c ^ (2 * j))) * kRowBytes);
+    unsigned r[4];
+    ldmatrix_x4(addr, r);
 #pragma unroll
-    for (int t = 0; t < OZK_NMAX; t++) {
-        if (t < N) emit(t, pack4(residue_bits<ND>(d0, t), residue_bits<ND>(d1, t), residue_bits<ND>(d2, t),
-                                 residue_bits<ND>(d3, t)));
-    }
-}
-
-template <typename Emit>
-__device__ __forceinline__ void quad_dispatch(int p, const double (&v)[4], const int (&ag)[4], int N, Emit emit) {
-    const int nd = (p + 1 + 9) / 10;   // X < 2^(p+1)
-    if (nd <= 6) quad_residues<6>(v, ag, N, emit);
-    else if (nd <= 7) quad_residues<7>(v, ag, N, emit);
-    else if (nd <= 8) quad_residues<8>(v, ag, N, emit);
-    else if (nd <= 10) quad_residues<10>(v, ag, N, emit);
-    else if (nd <= 12) quad_residues<12>(v, ag, N, emit);
-    else quad_residues<16>(v, ag, N, emit);
-}
-
-// A (m x k, row-major) -> Ares[t][i][l]: one thread per 4 consecutive l of a row; plane stores are coalesced
-__global__ void __launch_bounds__(256) split_a_kernel(const double* __restrict__ A, const int32_t* __restrict__ r,
-                                                      const int32_t* __restrict__ gam, const int32_t* __restrict__ p_dev,
-                                                      int m, int k, int N, int8_t* __restrict__ Ares) {
-    const long long quads = (long long)m * (k >> 2);
-    const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= quads) return;
-    const int k4 = k >> 2;
-    const int i = (int)(g / k4), l4 = (int)(g - (long long)i * k4);
-    const int p = *p_dev;
-    const double2* rowp = reinterpret_cast<const double2*>(A + (size_t)i * k) + 2 * l4;
-    const double2 a01 = __ldg(rowp), a23 = __ldg(rowp + 1);
-    const int4 gg = __ldg(reinterpret_cast<const int4*>(gam) + l4);
-    const int base = p - __ldg(r + i);
-    const double v[4] = {a01.x, a01.y, a23.x, a23.y};
-    const int ag[4] = {base + gg.x, base + gg.y, base + gg.z, base + gg.w};
-    const size_t plane = (size_t)m * k;
-    unsigned* out = reinterpret_cast<unsigned*>(Ares + (size_t)i * k) + l4;
-    quad_dispatch(p, v, ag, N, [&](int t, unsigned w) { out[(size_t)t * (plane >> 2)] = w; });
-}
-
-// B (k x n, row-major) -> Bres[t][j][l] (transposed): a block owns 32 rows l x 32 columns j; thread (j, quad of l)
-// computes 4 residues per plane into shared memory, then the block writes 32-byte K-contiguous runs per (t, j).
-constexpr int kBRows = 32, kBCols = 32, kBPitch = 9;   // words per (t, j) row of the smem tile: 8 + 1 pad
-
-__global__ void __launch_bounds__(256) split_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ c,
-                                                      const int32_t* __restrict__ gam, const int32_t* __restrict__ p_dev,
-                                                      int k, int n, int N, int8_t* __restrict__ Bres) {
-    __shared__ unsigned sm[OZK_NMAX * kBCols * kBPitch];
-    const int j0 = blockIdx.x * kBCols, l0 = blockIdx.y * kBRows;
-    const int jj = threadIdx.x & 31, lq = threadIdx.x >> 5;   // lq: quad 0..7 of the 32 rows
-    const int j = j0 + jj;
-    const int p = *p_dev;
-    const int base = p - __ldg(c + j);
-    double v[4];
-    int ag[4];
+    for (int i = 0; i < 4; i++) b[i] = r[i];
+    if (KB == 32) {
+        ldmatrix_x4(addr + kHalfBytes, r);
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-        const int l = l0 + 4 * lq + q;
-        v[q] = __ldg(B + (size_t)l * n + j);
-        ag[q] = base - __ldg(gam + l);
+        for (int i = 0; i < 4; i++) b[4 + i] = r[i];
     }
-    quad_dispatch(p, v, ag, N, [&](int t, unsigned w) { sm[(t * kBCols + jj) * kBPitch + lq] = w; });
-    __syncthreads();
-    // N planes x 32 columns x 2 chunks of 16 bytes
-    const int chunks = N * kBCols * 2;
-    for (int cidx = threadIdx.x; cidx < chunks; cidx += blockDim.x) {
-        const int t = cidx / (kBCols * 2), rem = cidx % (kBCols * 2), jr = rem >> 1, part = rem & 1;
-        const unsigned* src = sm + (t * kBCols + jr) * kBPitch + 4 * part;
-        const uint4 w = make_uint4(src[0], src[1], src[2], src[3]);
-        int8_t* dst = Bres + ((size_t)t * n + (j0 + jr)) * (size_t)k + l0 + 16 * part;
-        *reinterpret_cast<uint4*>(dst) = w;
+}
+
+// Residues of one chunk for the 16 moduli of a row tile; row A of lane (g, tig) is modulus t0 + g, row B modulus
+// t0 + g + 8.  `o` points at byte 8 tig of the chunk in plane 0.  Each pair of n-tiles gives one packed word per
+// row, so few products are live at a time.
+template <int KB>
+__device__ __forceinline__ void chunk_residues(const unsigned (&b)[KB / 4], const TileConsts<KB>& tc, int t0, int N,
+                                               int8_t* o, size_t plane_bytes) {
+    const int g = (threadIdx.x & 31) >> 2;
+    const bool needB = t0 + 8 < N;   // warp-uniform
+    const int hA = (int)((0u - tc.nPA) >> 1), hB = (int)((0u - tc.nPB) >> 1);   // floor(m / 2)
+    unsigned wA[2], wB[2];
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        unsigned rA[4], rB[4];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int nt = 2 * half + u;
+            int d1[4], d0[4];
+            if (KB == 16) {
+                mma_k16(d1, tc.a, b[nt], hA, hB);
+                mma_k16(d0, tc.a, b[nt], 0, 0);
+            } else {
+                mma_k32(d1, tc.a, b[nt], b[4 + nt], hA, hB);
+                mma_k32(d0, tc.a, b[nt], b[4 + nt], 0, 0);
+            }
+            rA[2 * u] = residue_byte(d1[0], d0[0], tc.MA, tc.nPA);
+            rA[2 * u + 1] = residue_byte(d1[1], d0[1], tc.MA, tc.nPA);
+            rB[2 * u] = needB ? residue_byte(d1[2], d0[2], tc.MB, tc.nPB) : 0u;
+            rB[2 * u + 1] = needB ? residue_byte(d1[3], d0[3], tc.MB, tc.nPB) : 0u;
+        }
+        wA[half] = pack4(rA[0], rA[1], rA[2], rA[3]);
+        wB[half] = pack4(rB[0], rB[1], rB[2], rB[3]);
     }
+    const int tA = t0 + g, tB = tA + 8;
+    if (tA < N) *reinterpret_cast<uint2*>(o + (size_t)tA * plane_bytes) = make_uint2(wA[0], wA[1]);
+    if (needB && tB < N) *reinterpret_cast<uint2*>(o + (size_t)tB * plane_bytes) = make_uint2(wB[0], wB[1]);
+}
+
+// One kernel for both operands.  A "vector" v is a row of A (v = i) or a column of B (v = j); its elements are
+// indexed by the contraction index l and its planes are out[t][v][l] (K-major).  A chunk is 32 consecutive l of one
+// vector (k % 32 == 0).  A warp task is TC chunks (TC = 8 for KB = 16, 4 for KB = 32), loaded with TC independent
+// 8-byte loads per lane:
+//   A: TC consecutive chunks of the row-major (v, l-block) order -- chunk ch covers A elements 32 ch .. 32 ch + 31
+//      and plane bytes 32 ch .. 32 ch + 31; lane L loads element L of each chunk (coalesced);
+//   B: TC adjacent columns of one l-block; lane (rg, c) = (lane / TC, lane % TC) loads rows TC rg + i (i < TC) of
+//      column c, so that each load instruction reads whole sectors.  Tasks run along l first, so the warps of a
+//      block write adjacent pieces of the same plane rows.
+template <int KB, bool IS_B>
+__device__ __forceinline__ void split_tasks(const double* __restrict__ src, const int32_t* __restrict__ vexp,
+                                            const int32_t* __restrict__ gam, int p, int V, int k, int N,
+                                            int8_t* __restrict__ out, unsigned char* wsm) {
+    constexpr int TC = KB == 16 ? OZK_SPLIT_TC16 : 4;     // chunks per task
+    constexpr int KW = KB / 4;               // words per byte string
+    constexpr int kChunkBytes = (KB / 16) * kHalfBytes + 16;
+    const int lane = threadIdx.x & 31, tig = lane & 3;
+    const int lblocks = k >> 5;
+    const size_t plane_bytes = (size_t)V * (size_t)k;
+    // chunk and task counts fit in 31 bits (checked on the host)
+    const int nchunks = V * lblocks;
+    const int ntasks = IS_B ? (V / TC) * lblocks : (nchunks + TC - 1) / TC;
+    const int gwarp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(wsm);
+    TileConsts<KB> tc0, tc1;
+    tc0.init(0);
+    tc1.init(16);
+    // task coordinates, advanced by the grid stride without divisions in the loop:
+    //   A: (v, lb) of the task's first chunk;  B: (vector group, l-block)
+    const int step = IS_B ? nwarps : nwarps * TC;
+    const int first = IS_B ? gwarp : gwarp * TC;
+    int cv = first / lblocks;
+    int clb = first - cv * lblocks;
+    const int sv = step / lblocks;
+    const int slb = step - sv * lblocks;
+    for (int task = gwarp; task < ntasks; task += nwarps) {
+        double x[TC];
+        int ag[TC];
+        int cnt = TC;
+        if (!IS_B) {
+            const int ch0 = task * TC;
+            cnt = nchunks - ch0 < TC ? nchunks - ch0 : TC;
+            int v = cv;
+            int lb = clb;
+#pragma unroll
+            for (int i = 0; i < TC; i++) {
+                if (i < cnt) {
+                    const int l = 32 * lb + lane;
+                    x[i] = __ldg(src + (size_t)(ch0 + i) * 32 + lane);
+                    ag[i] = p - __ldg(vexp + v) + __ldg(gam + l);
+                } else {
+                    x[i] = 0.0;
+                    ag[i] = 0;
+                }
+                if (++lb == lblocks) { lb = 0; v++; }
+            }
+        } else {
+            const int c = lane % TC, rg = lane / TC;
+            const int v = cv * TC + c;
+            const int cexp = p - __ldg(vexp + v);
+#pragma unroll
+            for (int i = 0; i < TC; i++) {
+                const int l = 32 * clb + TC * rg + i;
+                x[i] = __ldg(src + (size_t)l * V + v);
+                ag[i] = cexp - __ldg(gam + l);
+            }
+        }
+        __syncwarp();   // the previous task's ldmatrix reads are done before the strings are overwritten
+#pragma unroll
+        for (int i = 0; i < TC; i++) {
+            unsigned w[KW];
+            element_words<KW>(x[i], ag[i], w);
+            const int chunk = IS_B ? lane % TC : i;
+            const int e = IS_B ? TC * (lane / TC) + i : lane;
+            unsigned char* row = wsm + chunk * kChunkBytes + row_of_element(e) * kRowBytes;
+            *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
+            if (KB == 32) *reinterpret_cast<uint4*>(row + kHalfBytes) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        __syncwarp();
+        // all fragments of the task first: the ldmatrix asm orders memory, so loading them between the stores of
+        // consecutive chunks would serialise the chunks
+        unsigned b[TC][KB / 4];
+#pragma unroll
+        for (int i = 0; i < TC; i++) chunk_fragments<KB>(sbase + (uint32_t)(i * kChunkBytes), b[i]);
+#pragma unroll
+        for (int i = 0; i < TC; i++) {
+            if (i < cnt) {
+                int8_t* o = IS_B ? out + (size_t)(cv * TC + i) * k + 32 * clb + 8 * tig
+                                 : out + (size_t)(task * TC + i) * 32 + 8 * tig;
+                chunk_residues<KB>(b[i], tc0, 0, N, o, plane_bytes);
+                if (N > 16) chunk_residues<KB>(b[i], tc1, 16, N, o, plane_bytes);
+            }
+        }
+        cv += sv;
+        clb += slb;
+        if (clb >= lblocks) { clb -= lblocks; cv++; }
+    }
+}
+
+template <bool IS_B>
+__global__ void __launch_bounds__(kWarps * 32, OZK_SPLIT_MINB) split_kernel(const double* __restrict__ src,
+                                                               const int32_t* __restrict__ vexp,
+                                                               const int32_t* __restrict__ gam,
+                                                               const int32_t* __restrict__ p_dev, int V, int k, int N,
+                                                               int8_t* __restrict__ out) {
+    __shared__ __align__(16) unsigned char strings[kWarps][kWarpSmem];
+    const int p = *p_dev;
+    unsigned char* wsm = strings[threadIdx.x >> 5];
+    if (p <= 119) split_tasks<16, IS_B>(src, vexp, gam, p, V, k, N, out, wsm);
+    else split_tasks<32, IS_B>(src, vexp, gam, p, V, k, N, out, wsm);
+}
+
+int split_blocks(long long tasks) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long want = (tasks + kWarps - 1) / kWarps;
+    const long long cap = 8LL * sms;
+    return (int)(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
 }  // namespace
@@ -171,13 +348,11 @@ extern "C" int ozk_split_a(const double* A, const int32_t* r, const int32_t* gam
                            int N, int8_t* Ares, ozk_stream_t stream_) {
     if (!A || !r || !gam || !p_dev || !Ares) return OZK_ERR_ARG;
     if (m <= 0 || k <= 0 || (k & 31) || N < 1 || N > OZK_NMAX) return OZK_ERR_ARG;
-    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Ares) | reinterpret_cast<uintptr_t>(gam)) & 15)
-        return OZK_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Ares)) & 15) return OZK_ERR_ARG;
+    if ((long long)m * (k >> 5) >= 0x7fffffffLL - (1LL << 24)) return OZK_ERR_ARG;   // chunk indices in 31 bits
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
-    const long long quads = (long long)m * (k >> 2);
-    const long long blocks = (quads + 255) / 256;
-    if (blocks > 0x7fffffffLL) return OZK_ERR_ARG;
-    split_a_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares);
+    const long long tasks = ((long long)m * (k >> 5) + 7) / 8;
+    split_kernel<false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }
@@ -187,8 +362,10 @@ extern "C" int ozk_split_b(const double* B, const int32_t* c, const int32_t* gam
     if (!B || !c || !gam || !p_dev || !Bres) return OZK_ERR_ARG;
     if (n <= 0 || k <= 0 || (k & 31) || (n & 31) || N < 1 || N > OZK_NMAX) return OZK_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(Bres) & 15) return OZK_ERR_ARG;
+    if ((long long)n * (k >> 5) >= 0x7fffffffLL - (1LL << 24)) return OZK_ERR_ARG;   // chunk indices in 31 bits
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
-    split_b_kernel<<<dim3(n / kBCols, k / kBRows), 256, 0, st>>>(B, c, gam, p_dev, k, n, N, Bres);
+    const long long tasks = (long long)(n / 8) * (k >> 5);
+    split_kernel<true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }

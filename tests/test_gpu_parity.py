@@ -222,6 +222,23 @@ def test_split_all_digit_widths(pkg, oracle, torch_mod, p):
     assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, 32))
 
 
+# ragged work division: row-block counts that leave a partial task, fewer l-blocks than chunks per task, every
+# plane-count boundary of the 16-modulus row tiles, both byte-string widths
+@pytest.mark.parametrize("m,k,n,N,p", [(12, 96, 32, 6, 40), (20, 64, 64, 8, 58), (36, 32, 96, 9, 60),
+                                       (12, 160, 32, 16, 70), (44, 96, 32, 17, 67), (8, 224, 64, 24, 90),
+                                       (28, 96, 32, 25, 119), (12, 96, 64, 20, 120), (16, 32, 32, 31, 150)])
+def test_split_ragged(pkg, oracle, torch_mod, m, k, n, N, p):
+    torch = torch_mod
+    A, B = pkg.make_inputs(m, k, n, 1.5, seed=m + k + N)
+    A[0, 0], B[1, 0] = -0.0, -3e-320
+    Ad, Bd = T(torch, A), T(torch, B)
+    st = dev_stats(pkg, torch, Ad, Bd)
+    sto = oracle.stats(A, B, True)
+    Ar, Br = dev_split(pkg, torch, Ad, Bd, st, p, N)
+    assert np.array_equal(Ar, oracle.split_A(A, sto["r"], sto["gam"], p, N))
+    assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, N))
+
+
 # ------------------------------------------------------------------------------------------------ INT8 products
 def rand_planes(rng, N, rows, k):
     return rng.integers(-128, 128, size=(N, rows, k), dtype=np.int64).astype(np.int8)
