@@ -79,6 +79,19 @@ int ozk_stats_finish(const double* A, const double* B, int m, int n, int k, int 
                      int32_t* gam, int32_t* r, int32_t* c, double* sA, double* nA, double* sB, double* nB,
                      int32_t* flag, void* workspace, size_t workspace_bytes, ozk_stream_t stream);
 
+/* One operand's statistics for a given gamma[k] (inside scaling already decided), for the persistent fixed
+ * operand mode (the reference's PersistA, ozaki_engine.py:2417-2466, which launches rowstatsA_k alone in encode,
+ * :2433-2442, and colexpB_k + colsumsB_k alone in _stats_B, :2444-2454, with gamma = 0):
+ *   ozk_stats_rows: r[m], sA[m], nA[m] of A (rowstatsA_k, :904-925);
+ *   ozk_stats_cols: c[n], sB[n], nB[n] of B (colexpB_k + colsumsB_k, :926-951), scratch of
+ *                   ozk_stats_cols_workspace_bytes(k, n) bytes (ozk_stats_workspace_bytes(m, n, k) is enough).
+ * Outputs equal those of ozk_stats for the same gamma.                                                       */
+int ozk_stats_rows(const double* A, int m, int k, const int32_t* gam, int32_t* r, double* sA, double* nA,
+                   ozk_stream_t stream);
+size_t ozk_stats_cols_workspace_bytes(int k, int n);
+int ozk_stats_cols(const double* B, int k, int n, const int32_t* gam, int32_t* c, double* sB, double* nB,
+                   void* workspace, size_t workspace_bytes, ozk_stream_t stream);
+
 /* Stage 1 without a workspace argument, for callers that cannot allocate device memory (they only hold device
  * pointers handed to them by another runtime, or must not call cudaMalloc while they run or record a CUDA graph).
  * This entry point has no counterpart in the reference.  Its scratch is a static device array of
@@ -154,6 +167,22 @@ int ozk_reconstruct(const uint8_t* X, const int32_t* r, const int32_t* c, const 
 int ozk_core(const double* A, const double* B, const int32_t* gam, const int32_t* r, const int32_t* c,
              const int32_t* p_dev, int m, int n, int k, int N, int skip_a, int8_t* Ares, int8_t* Bres, uint8_t* X,
              double* C, int32_t* err, ozk_stream_t stream);
+
+/* ---- full-matrix certificate of the plane count (replaces full_certificate, ozaki_engine.py:1542-1583) --- *
+ * For the statistics gam, r, c, sA, sB of the problem (inside scaling on): a lower bound of
+ * D_ij = sum_l |A_il||B_lj| on every entry from one FP16 tensor-core product (tcgen05.mma kind::f16, FP32
+ * accumulation) of the magnitudes scaled by 2^(gamma_l - r_i) and 2^(-c_j - gamma_l) and rounded down by
+ * (1 - 2^-10), derated by (1 - 8 k 2^-24); for every entry with D > 0 the largest x with
+ * F1 x + F2 x^2 <= tau D / safety (F1 = (2^r_i sB_j + 2^c_j sA_i) / 2, F2 = k 2^(r_i + c_j) / 4).
+ * Outputs (device): xmin[0] = min of that x over the entries with D > 0 (all bits set when there is none; the
+ * required p is ceil(-log2(xmin) + 1e-9)), uncertified[0] = number of entries with D not > 0.  D_out (optional,
+ * m x n, may be NULL) receives D.  Scratch: ozk_certificate_workspace_bytes(m, n, k), 256-byte aligned.
+ * err: device int32, OR'ed OZK_DEVERR_* flags of the bounded waits.                                          */
+size_t ozk_certificate_workspace_bytes(int m, int n, int k);
+int ozk_certificate(const double* A, const double* B, int m, int n, int k, const int32_t* gam, const int32_t* r,
+                    const int32_t* c, const double* sA, const double* sB, double tau, double safety, double* xmin,
+                    uint64_t* uncertified, double* D_out, int32_t* err, void* workspace, size_t workspace_bytes,
+                    ozk_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -23,12 +23,18 @@ def __getattr__(name):
     if name in ("DistributedOzakiCRT",):
         from . import distributed
         return getattr(distributed, name)
+    if name in ("PersistA",):
+        from . import persist
+        return getattr(persist, name)
+    if name in ("full_certificate",):
+        from . import certificate
+        return getattr(certificate, name)
     if name in ("make_inputs", "config_inputs", "Sample", "exact_sample", "CONFIGS"):
         from . import harness
         return getattr(harness, name)
     raise AttributeError(name)
 
 
-__all__ = ["OzakiCRT", "DistributedOzakiCRT", "MODS", "NMAX", "NEG", "pmax_bits", "bound_matrix", "worst_case_p",
+__all__ = ["OzakiCRT", "DistributedOzakiCRT", "PersistA", "full_certificate", "MODS", "NMAX", "NEG", "pmax_bits", "bound_matrix", "worst_case_p",
            "sigma_of", "make_config_table", "pick_config", "limbs_for", "_limbs_for", "_pow2tab", "modulus_product",
            "make_inputs", "config_inputs", "Sample", "exact_sample", "CONFIGS", "_lib"]

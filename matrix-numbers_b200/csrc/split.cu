@@ -13,7 +13,7 @@
 // and lies in [0, 2^21]:
 // for a warp chunk of 32 elements the sums of all moduli are one small integer matrix product,
 // [16 moduli x KB bytes] x [KB bytes x 32 elements], run as mma.m16n8k16 / m16n8k32 (u8 x u8 -> s32, exact) on the
-// byte strings staged in shared memory and loaded with ldmatrix.  The MMA runs twice, accumulating onto h_t
+// byte strings staged in shared memory.  The MMA runs twice, accumulating onto h_t
 // (m_t / 2 for m_t = 256, (m_t - 1) / 2 for odd m_t) and onto 0: q = floor((s + h) / m_t) is one multiply-high by
 // ceil(2^32 / m_t) (exact for s + h < 2^24), and the low byte of s - m_t q is the symmetric residue -- two integer
 // instructions per residue, no per-modulus digit sums and no sign handling.  The element -> MMA column assignment
@@ -62,7 +62,7 @@ __constant__ SplitTables c_split = make_split_tables();
 #endif
 
 constexpr int kWarps = 8;                            // warps per block
-constexpr int kRowBytes = 16;                        // one ldmatrix row: 16 bytes of an element's byte string
+constexpr int kRowBytes = 16;                        // 16 bytes of an element's byte string
 constexpr int kHalfBytes = 32 * kRowBytes;           // one 16-byte half of the strings of a 32-element chunk
 constexpr int kWarpSmem = 8 * (kHalfBytes + 16);     // 8 chunks of KB = 16 (or 4 of KB = 32) per warp, padded
 
@@ -89,12 +89,12 @@ __device__ __forceinline__ void element_words(double v, int ag, unsigned (&w)[KW
     const unsigned E = (hi >> 20) & 0x7FFu;
     const unsigned long long mant = ((unsigned long long)((hi & 0xFFFFFu) | (E ? 0x100000u : 0u)) << 32) | lo;
     const int s = (int)(E ? E : 1u) - 1075 + ag;
-    const unsigned long long xr = (shr64(mant, (unsigned)(-s - 1)) + 1ULL) >> 1;   // s < 0
-    const unsigned long long x = s < 0 ? xr : mant;
-    const int sh = s < 0 ? 0 : s;
+    const unsigned long long xr = (shr64(mant, (unsigned)(-s - 1)) + 1ULL) >> 1;   // s < 0: below 2^54, one limb
 #pragma unroll
     for (int j = 0; j < KW / 2; j++) {
-        const unsigned long long limb = shl64(x, (unsigned)(sh - 64 * j)) | shr64(x, (unsigned)(64 * j - sh));
+        unsigned long long limb = shl64(mant, (unsigned)(s - 64 * j)) | shr64(mant, (unsigned)(64 * j - s));
+        if (j == 0) limb = s < 0 ? xr : limb;
+        else limb = s < 0 ? 0ULL : limb;
         w[2 * j] = (unsigned)limb;
         w[2 * j + 1] = (unsigned)(limb >> 32);
     }
@@ -104,20 +104,13 @@ __device__ __forceinline__ void element_words(double v, int ag, unsigned (&w)[KW
     w[KW - 1] = (w[KW - 1] & 0x00FFFFFFu) | ((hi >> 7) & 0x01000000u);
 }
 
-// Shared-memory row of element e (0..31) of a chunk: ldmatrix matrix j (n-tile j) reads rows 8j .. 8j+7, and row
+// Shared-memory row of element e (0..31) of a chunk: the fragments of n-tile j come from rows 8j .. 8j+7, and row
 // 8j + (c ^ 2j) holds element 8(c >> 1) + 2j + (c & 1), so that the MMA column pairs (2 tig, 2 tig + 1) of the four
 // n-tiles are elements 8 tig .. 8 tig + 7.  The XOR keeps both the row writes of 8 consecutive elements and the 8
-// rows of an ldmatrix matrix on distinct 16-byte bank groups.
+// rows of an n-tile on distinct 16-byte bank groups.
 __device__ __forceinline__ int row_of_element(int e) {
     const int j = (e >> 1) & 3;
     return 8 * j + (((e & 1) + 2 * (e >> 3)) ^ (2 * j));
-}
-
-__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, unsigned (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr)
-                 : "memory");
 }
 
 __device__ __forceinline__ void mma_k16(int (&d)[4], const unsigned* a, unsigned b0, int cA, int cB) {
@@ -131,10 +124,6 @@ __device__ __forceinline__ void mma_k32(int (&d)[4], const unsigned* a, unsigned
         "{%10, %11, %12, %13};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(cA), "r"(cA), "r"(cB), "r"(cB));
-}
-
-__device__ __forceinline__ unsigned pack4(unsigned b0, unsigned b1, unsigned b2, unsigned b3) {
-    return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
 }
 
 // Per-lane constants of one 16-modulus row tile (moduli t0 + g and t0 + g + 8 of lane (g, tig)).  The lane-dependent
@@ -162,25 +151,30 @@ struct TileConsts {
     }
 };
 
-// low byte of s - m floor((s + h) / m), from sh = s + h and s
-__device__ __forceinline__ unsigned residue_byte(int sh, int s, unsigned M, unsigned nP) {
-    return __umulhi((unsigned)sh, M) * nP + (unsigned)s;
+// s - m floor((s + h) / m) in [-128, 127], from sh = s + h and s
+__device__ __forceinline__ int residue(int sh, int s, unsigned M, unsigned nP) {
+    return (int)(__umulhi((unsigned)sh, M) * nP + (unsigned)s);
 }
 
-// B fragments of a chunk (32 elements, byte strings at shared address `chunk`): four n-tiles, k 0-15 (and 16-31)
+// four residues in [-128, 127] as the bytes (r0, r1, r2, r3) of a word
+__device__ __forceinline__ unsigned pack_s8(int r0, int r1, int r2, int r3) {
+    unsigned hi, w;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(r3), "r"(r2));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(r1), "r"(r0), "r"(hi));
+    return w;
+}
+
+// B fragments of a chunk (32 elements, byte strings at `chunk` in shared memory): for n-tile j, lane (g, tig) needs
+// word tig of element 8(g >> 1) + 2j + (g & 1), stored in row 8j + (g ^ 2j) (k 0-15; k 16-31 in the second half).
+// Plain 32-bit shared loads (a warp reads 8 whole rows, conflict-free), which the compiler can schedule freely.
 template <int KB>
-__device__ __forceinline__ void chunk_fragments(uint32_t chunk, unsigned (&b)[KB / 4]) {
-    const int lane = threadIdx.x & 31;
-    const int j = lane >> 3, c = lane & 7;
-    const uint32_t addr = chunk + (uint32_t)((8 * j + (c ^ (2 * j))) * kRowBytes);
-    unsigned r[4];
-    ldmatrix_x4(addr, r);
+__device__ __forceinline__ void chunk_fragments(const unsigned char* chunk, unsigned (&b)[KB / 4]) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
 #pragma unroll
-    for (int i = 0; i < 4; i++) b[i] = r[i];
-    if (KB == 32) {
-        ldmatrix_x4(addr + kHalfBytes, r);
-#pragma unroll
-        for (int i = 0; i < 4; i++) b[4 + i] = r[i];
+    for (int j = 0; j < 4; j++) {
+        const unsigned* row = reinterpret_cast<const unsigned*>(chunk + (8 * j + (g ^ (2 * j))) * kRowBytes);
+        b[j] = row[tig];
+        if (KB == 32) b[4 + j] = row[kHalfBytes / 4 + tig];
     }
 }
 
@@ -196,7 +190,7 @@ __device__ __forceinline__ void chunk_residues(const unsigned (&b)[KB / 4], cons
     unsigned wA[2], wB[2];
 #pragma unroll
     for (int half = 0; half < 2; half++) {
-        unsigned rA[4], rB[4];
+        int rA[4], rB[4];
 #pragma unroll
         for (int u = 0; u < 2; u++) {
             const int nt = 2 * half + u;
@@ -208,13 +202,13 @@ __device__ __forceinline__ void chunk_residues(const unsigned (&b)[KB / 4], cons
                 mma_k32(d1, tc.a, b[nt], b[4 + nt], hA, hB);
                 mma_k32(d0, tc.a, b[nt], b[4 + nt], 0, 0);
             }
-            rA[2 * u] = residue_byte(d1[0], d0[0], tc.MA, tc.nPA);
-            rA[2 * u + 1] = residue_byte(d1[1], d0[1], tc.MA, tc.nPA);
-            rB[2 * u] = needB ? residue_byte(d1[2], d0[2], tc.MB, tc.nPB) : 0u;
-            rB[2 * u + 1] = needB ? residue_byte(d1[3], d0[3], tc.MB, tc.nPB) : 0u;
+            rA[2 * u] = residue(d1[0], d0[0], tc.MA, tc.nPA);
+            rA[2 * u + 1] = residue(d1[1], d0[1], tc.MA, tc.nPA);
+            rB[2 * u] = needB ? residue(d1[2], d0[2], tc.MB, tc.nPB) : 0;
+            rB[2 * u + 1] = needB ? residue(d1[3], d0[3], tc.MB, tc.nPB) : 0;
         }
-        wA[half] = pack4(rA[0], rA[1], rA[2], rA[3]);
-        wB[half] = pack4(rB[0], rB[1], rB[2], rB[3]);
+        wA[half] = pack_s8(rA[0], rA[1], rA[2], rA[3]);
+        wB[half] = pack_s8(rB[0], rB[1], rB[2], rB[3]);
     }
     const int tA = t0 + g, tB = tA + 8;
     if (tA < N) *reinterpret_cast<uint2*>(o + (size_t)tA * plane_bytes) = make_uint2(wA[0], wA[1]);
@@ -245,7 +239,6 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
     const int ntasks = IS_B ? (V / TC) * lblocks : (nchunks + TC - 1) / TC;
     const int gwarp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
-    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(wsm);
     TileConsts<KB> tc0, tc1;
     tc0.init(0);
     tc1.init(16);
@@ -289,7 +282,7 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
                 ag[i] = cexp - __ldg(gam + l);
             }
         }
-        __syncwarp();   // the previous task's ldmatrix reads are done before the strings are overwritten
+        __syncwarp();   // the previous task's fragment reads are done before the strings are overwritten
 #pragma unroll
         for (int i = 0; i < TC; i++) {
             unsigned w[KW];
@@ -301,18 +294,15 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
             if (KB == 32) *reinterpret_cast<uint4*>(row + kHalfBytes) = make_uint4(w[4], w[5], w[6], w[7]);
         }
         __syncwarp();
-        // all fragments of the task first: the ldmatrix asm orders memory, so loading them between the stores of
-        // consecutive chunks would serialise the chunks
-        unsigned b[TC][KB / 4];
-#pragma unroll
-        for (int i = 0; i < TC; i++) chunk_fragments<KB>(sbase + (uint32_t)(i * kChunkBytes), b[i]);
 #pragma unroll
         for (int i = 0; i < TC; i++) {
             if (i < cnt) {
                 int8_t* o = IS_B ? out + (size_t)(cv * TC + i) * k + 32 * clb + 8 * tig
                                  : out + (size_t)(task * TC + i) * 32 + 8 * tig;
-                chunk_residues<KB>(b[i], tc0, 0, N, o, plane_bytes);
-                if (N > 16) chunk_residues<KB>(b[i], tc1, 16, N, o, plane_bytes);
+                unsigned b[KB / 4];
+                chunk_fragments<KB>(wsm + i * kChunkBytes, b);
+                chunk_residues<KB>(b, tc0, 0, N, o, plane_bytes);
+                if (N > 16) chunk_residues<KB>(b, tc1, 16, N, o, plane_bytes);
             }
         }
         cv += sv;

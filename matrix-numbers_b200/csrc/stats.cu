@@ -244,6 +244,43 @@ extern "C" int ozk_stats_finish(const double* A, const double* B, int m, int n, 
     return OZK_OK;
 }
 
+extern "C" int ozk_stats_rows(const double* A, int m, int k, const int32_t* gam, int32_t* r, double* sA, double* nA,
+                              ozk_stream_t stream_) {
+    if (!A || !gam || !r || !sA || !nA) return OZK_ERR_ARG;
+    if (m <= 0 || k <= 0 || (k & 1)) return OZK_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(gam)) & 15) return OZK_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    rowstats_a_kernel<<<m, kThreads, 0, st>>>(A, gam, k, r, sA, nA);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}
+
+extern "C" size_t ozk_stats_cols_workspace_bytes(int k, int n) {
+    if (n <= 0 || k <= 0) return 0;
+    const size_t nchunks = ((size_t)k + kColChunk - 1) / kColChunk;
+    return align256(nchunks * (size_t)n * 8) * 2 + align256(nchunks * (size_t)n * 4);
+}
+
+extern "C" int ozk_stats_cols(const double* B, int k, int n, const int32_t* gam, int32_t* c, double* sB, double* nB,
+                              void* workspace, size_t workspace_bytes, ozk_stream_t stream_) {
+    if (!B || !gam || !c || !sB || !nB || !workspace) return OZK_ERR_ARG;
+    if (n <= 0 || k <= 0 || (n & 1)) return OZK_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(B) & 15) return OZK_ERR_ARG;
+    if (workspace_bytes < ozk_stats_cols_workspace_bytes(k, n)) return OZK_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    const int nchunks = (k + kColChunk - 1) / kColChunk;
+    char* ws = static_cast<char*>(workspace);
+    double* ps = reinterpret_cast<double*>(ws);
+    double* pq = reinterpret_cast<double*>(ws + align256((size_t)nchunks * n * 8));
+    int32_t* pc = reinterpret_cast<int32_t*>(ws + 2 * align256((size_t)nchunks * n * 8));
+    const dim3 g2((n / 2 + kThreads - 1) / kThreads, nchunks);
+    colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, pc, ps, pq);
+    OZK_CHECK_LAUNCH();
+    colstats_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}
+
 extern "C" int ozk_stats(const double* A, const double* B, int m, int n, int k, int inside, int32_t* gam, int32_t* r,
                          int32_t* c, double* sA, double* nA, double* sB, double* nB, int32_t* flag, void* workspace,
                          size_t workspace_bytes, ozk_stream_t stream) {

@@ -258,6 +258,8 @@ class OzakiCRT:
         self._shape_check(A, B, C)
         m, k = A.shape
         n = B.shape[1]
+        if force_N is not None and force_p is not None:
+            return self._run_config(A, B, C, tau, safety, inside, int(force_N), int(force_p), events)
         b = self.buffers(m, n, k, 20)
         key = ("sr", m, n, k, A.data_ptr(), B.data_ptr(), tau, safety, inside, force_N, force_p)
         g = self.graphs.get(key)
@@ -290,6 +292,49 @@ class OzakiCRT:
         self.core_graph(A, B, b, N, C)
         mark("core")
         return C, {"N": N, "p": p, "preq": preq}
+
+    def _run_config(self, A, B, C, tau, safety, inside, N, p, events=None):
+        """Configuration-table fast path (N and p both given, e.g. by pick_config): ONE graph of statistics, the
+        forced rule (no probe product), the core for N planes and the copy of the decision to pinned host memory,
+        then one synchronisation.  The reference's graph path reads (N, p) on the host between two graphs
+        (ozaki_engine.py:1432-1457); with N known beforehand nothing in the core depends on that read.  If the
+        forced rule rejects the configuration (p above the data's exact range) or the input is not finite, the
+        core's output is discarded and C is recomputed natively, as the reference does."""
+        m, k = A.shape
+        n = B.shape[1]
+        if not 1 <= N <= NMAX:
+            torch.matmul(A, B, out=C)
+            return C, {"fallback": True, "preq": 0}
+        b = self.buffers(m, n, k, N)
+        key = ("cfg", m, n, k, A.data_ptr(), B.data_ptr(), C.data_ptr(), tau, safety, inside, N, p)
+        g = self.graphs.get(key)
+        if g is None:
+            def body():
+                self._stats_rule(A, B, b, tau, safety, inside, N, p)
+                self.core(A, B, b, N, C)
+                b["hctl"].copy_(b["ctl"], non_blocking=True)
+            g = self._capture(body)
+            self.graphs[key] = g
+        if events is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            events.append(("start", e))
+        g.replay()
+        self.launches += 14
+        torch.cuda.current_stream().synchronize()
+        if events is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            events.append(("stats+rule+core", e))
+        ctl = [int(x) for x in b["hctl"].tolist()]
+        if ctl[4]:
+            raise _lib.OzkError(f"device error flag {ctl[4]:#x} raised by an INT8 GEMM launch (a bounded wait ran "
+                                "out); the result is invalid")
+        Nd, pd, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
+        if fb or Nd == 0:
+            torch.matmul(A, B, out=C)
+            return C, {"fallback": True, "preq": preq}
+        return C, {"N": Nd, "p": pd, "preq": preq}
 
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, graph=False, prof=None, seed=0, config=None,
             force_p=None):

@@ -280,6 +280,53 @@ def run(A, B, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, s
 
 
 # ------------------------------------------------------------------ the exact sampled reference (measurement)
+def persist_product(A, B, N, p):
+    """One product of the persistent fixed operand mode (PersistA, ozaki_engine.py:2417-2466) on the CPU: A encoded
+    at (N, p) with gamma = 0 (encode, :2433-2442), B's column statistics with gamma = 0, the forced rule for (N, p)
+    (_stats_B -> _rule_device, :2444-2454, :1387-1396: p_B = min(pmax_bits(N, nu_A, nu_B, k), p), fallback flag when
+    that is below p), then core with skipA: B residues and reconstruction at p_B, the A planes kept at p.
+    Returns (C, {"p_B", "fallback"})."""
+    A, B = _c64(A), _c64(B)
+    m, k = A.shape
+    n = B.shape[1]
+    st = stats(A, B, inside=False)                         # gamma = 0: the row and column statistics of encode/_stats_B
+    nuA, nuB = math.sqrt(float(np.max(st["nA"]))), math.sqrt(float(np.max(st["nB"])))
+    pv = pmax_bits(N, nuA, nuB, k)
+    pB = min(pv, int(p))
+    Ares = split_A(A, st["r"], st["gam"], p, N)
+    Bres = split_B(B, st["c"], st["gam"], pB, N)
+    C = recon(gemm_mod(Ares, Bres), st["r"], st["c"], pB)
+    return C, {"p_B": pB, "fallback": pv < int(p)}
+
+
+def full_certificate(A, B, st, tau=2.0 ** -52, safety=2.0):
+    """The reference's full_certificate arithmetic (ozaki_engine.py:1542-1583) in numpy: FP16 magnitudes scaled by
+    2^(gamma - r) and 2^(-c - gamma), rounded down by (1 - 2^-10) and converted through float32 as torch's
+    .to(float16) does; their product summed in float64 (the reference sums in FP32 on the tensor cores: both sums
+    differ from the exact one by far less than the 8 k 2^-24 derating); the bound of every entry; the maximum need.
+    Returns need, preq, uncertified and the matrices D (derated lower bound) and xmax."""
+    A, B = _c64(A), _c64(B)
+    m, k = A.shape
+    r = np.asarray(st["r"], np.int64)
+    c = np.asarray(st["c"], np.int64)
+    gam = np.asarray(st["gam"], np.int64)
+    g = np.ldexp(1.0, gam)
+    As = (np.abs(A) * (g[None, :] * np.ldexp(1.0, -r)[:, None]) * (1 - 2.0 ** -10)).astype(np.float32).astype(np.float16)
+    Bs = (np.abs(B) * (np.ldexp(1.0, -c)[None, :] / g[:, None]) * (1 - 2.0 ** -10)).astype(np.float32).astype(np.float16)
+    Dl = As.astype(np.float64) @ Bs.astype(np.float64)
+    rI, cJ = np.ldexp(1.0, r)[:, None], np.ldexp(1.0, c)[None, :]
+    D = Dl * (1 - 8 * k * 2.0 ** -24) * rI * cJ
+    F1 = 0.5 * (rI * np.asarray(st["sB"])[None, :] + cJ * np.asarray(st["sA"])[:, None])
+    F2 = 0.25 * k * rI * cJ
+    thr = tau * D / safety
+    mask = D > 0
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        xmax = 2 * thr / (F1 + np.sqrt(F1 * F1 + 4 * F2 * thr))
+        need = float(np.where(mask, -np.log2(xmax), -1e30).max())
+    return {"need": need, "preq": int(math.ceil(need + 1e-9)), "uncertified": int((~mask).sum()), "D": D,
+            "xmax": xmax}
+
+
 def _split(a):
     t = 134217729.0 * a
     hi = t - (t - a)

@@ -1,0 +1,88 @@
+"""Full-matrix certificate (reference full_certificate, code/ozaki_engine.py:1542-1583): the tcgen05 FP16 kernel with
+the bound reduced in its epilogue, against the numpy restatement of the reference arithmetic (oracle.full_certificate).
+
+The FP16 operands are bit-identical to the reference's; the product is summed in FP32 on the tensor cores in a
+different order than cuBLAS (and than the oracle's float64 sum), so D agrees to within the FP32 accumulation error,
+which the certificate's 8 k 2^-24 derating covers: D must stay below the exact sum of |A||B| on every entry."""
+import numpy as np
+import pytest
+
+
+def test_oracle_certificate_is_a_lower_bound(pkg, oracle):
+    A, B = pkg.make_inputs(48, 256, 64, 2.0, seed=9)
+    B[:, 3] = 0.0
+    st = oracle.stats(A, B, True)
+    cert = oracle.full_certificate(A, B, st)
+    exact = np.abs(A) @ np.abs(B)
+    assert np.all(cert["D"][exact > 0] <= exact[exact > 0])
+    assert cert["uncertified"] == 48                      # the zero column
+    assert np.all(cert["D"][:, 3] == 0)
+
+
+def _dev_stats(torch, E, Ad, Bd):
+    m, k = Ad.shape
+    b = E.buffers(m, Bd.shape[1], k, 20)
+    E.stats(Ad, Bd, b, True)
+    return b
+
+
+def _tol(k):
+    return 3.0 * (k + 2) * 2.0 ** -24
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,k,n,phi", [(128, 256, 256, 1.0), (260, 544, 96, 2.0), (512, 2048, 384, 0.5),
+                                       (64, 96, 512, 3.0)])
+def test_certificate_kernel_vs_oracle(pkg, oracle, engine, m, k, n, phi):
+    import torch
+    from matrix_numbers_b200.certificate import certificate_device, required_p
+    A, B = pkg.make_inputs(m, k, n, phi, seed=m + n)
+    A[5, :] = 0.0
+    B[:, 7] = 0.0
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    b = _dev_stats(torch, engine, Ad, Bd)
+    st = oracle.stats(A, B, True)
+    Dd = torch.empty(m, n, dtype=torch.float64, device="cuda")
+    w = certificate_device(engine, Ad, Bd, b["gam"], b["r"], b["c"], b["sA"], b["sB"], D_out=Dd)
+    torch.cuda.synchronize()
+    assert int(w["err"].item()) == 0
+    ref = oracle.full_certificate(A, B, st)
+    D = Dd.cpu().numpy()
+    exact = np.abs(A) @ np.abs(B)
+    pos = ref["D"] > 0
+    assert np.array_equal(D > 0, pos)
+    assert int(w["unc"].item()) == ref["uncertified"] == int((~pos).sum())
+    rel = np.abs(D[pos] - ref["D"][pos]) / ref["D"][pos]
+    assert rel.max() <= _tol(k)
+    # a lower bound of the exact sum wherever the reference's arithmetic gives one: its FP16 rounding of magnitudes in
+    # the subnormal range (below 2^-14) can round up by far more than the (1 - 2^-10) pre-scaling (at phi = 3 one
+    # entry of the restatement exceeds the exact sum by 0.8%); there the kernel must agree with the restatement
+    ok_ref = ref["D"][pos] <= exact[pos]
+    assert np.all(D[pos][ok_ref] <= exact[pos][ok_ref] * (1 + 2.0 ** -40))
+    assert ok_ref.mean() > 0.99
+    preq, need = required_p(int(w["xmin"].view(torch.int64).item()))
+    assert abs(need - ref["need"]) <= _tol(k)
+    frac = ref["need"] + 1e-9 - np.floor(ref["need"] + 1e-9)
+    if _tol(k) < frac < 1 - _tol(k):                         # not within the tolerance of an integer boundary
+        assert preq == ref["preq"]
+
+
+@pytest.mark.gpu
+def test_full_certificate_api(pkg, oracle, engine):
+    import torch
+    m, k, n = 256, 1024, 256
+    A, B = pkg.make_inputs(m, k, n, 2.0, seed=4)
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    C, info = engine.run(Ad, Bd)
+    cert = pkg.full_certificate(engine, Ad, Bd, info)
+    assert set(cert) == {"N_full", "preq_full", "preq_sampled", "uncertified_entries", "cost_ms", "N_sampled",
+                         "sampled_config_fully_certified"}
+    ref = oracle.full_certificate(A, B, oracle.stats(A, B, True))
+    assert abs(cert["preq_full"] - ref["preq"]) <= 1
+    assert cert["uncertified_entries"] == ref["uncertified"] == 0
+    assert cert["preq_sampled"] == info["p_req"] and cert["N_sampled"] == info["N"]
+    assert cert["preq_full"] >= info["p_req"] - 1          # every probe entry is one of the certified entries
+    Nf = cert["N_full"]
+    assert Nf is not None and pkg.pmax_bits(Nf, info["nuA"], info["nuB"], k) >= cert["preq_full"]
+    assert Nf == 6 or pkg.pmax_bits(Nf - 1, info["nuA"], info["nuB"], k) < cert["preq_full"]
+    assert cert["sampled_config_fully_certified"] == (info["N"] >= Nf)
