@@ -29,6 +29,9 @@ def __getattr__(name):
     if name in ("full_certificate",):
         from . import certificate
         return getattr(certificate, name)
+    if name in ("coprime_ip", "int8_crt", "chain_cost_model"):
+        from . import planning
+        return getattr(planning, name)
     if name in ("make_inputs", "config_inputs", "Sample", "exact_sample", "CONFIGS"):
         from . import harness
         return getattr(harness, name)
@@ -37,4 +40,5 @@ def __getattr__(name):
 
 __all__ = ["OzakiCRT", "DistributedOzakiCRT", "PersistA", "full_certificate", "MODS", "NMAX", "NEG", "pmax_bits", "bound_matrix", "worst_case_p",
            "sigma_of", "make_config_table", "pick_config", "limbs_for", "_limbs_for", "_pow2tab", "modulus_product",
-           "make_inputs", "config_inputs", "Sample", "exact_sample", "CONFIGS", "_lib"]
+           "make_inputs", "config_inputs", "Sample", "exact_sample", "CONFIGS", "coprime_ip", "int8_crt",
+           "chain_cost_model", "_lib"]
