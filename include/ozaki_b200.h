@@ -184,6 +184,14 @@ int ozk_certificate(const double* A, const double* B, int m, int n, int k, const
                     uint64_t* uncertified, double* D_out, int32_t* err, void* workspace, size_t workspace_bytes,
                     ozk_stream_t stream);
 
+/* The plane-count rule driven by the certificate instead of the probe (the certified variant of the rule in the
+ * timed path, from the reference's full_certificate, :1570-1575): p_req = ceil(-log2(xmin) + 1e-9) clamped to
+ * [1, 1000] (xmin from ozk_certificate), N = the smallest N in [6, 32] with pmax_bits(N, nu_A, nu_B, k) >= p_req;
+ * dec[4] = {N (0 on fallback), p = pmax_bits(N, ..), fallback, p_req}, p_dev[1] = p, aux[8] = {nuA, nuB,
+ * -log2(xmin), 0...}.  Fallback on a non-finite flag, no such N, or p_req > 249.                             */
+int ozk_rule_certified(const double* nA, const double* nB, const int32_t* flag, int m, int n, int k,
+                       const double* xmin, int32_t* dec, int32_t* p_dev, double* aux, ozk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

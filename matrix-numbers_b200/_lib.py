@@ -37,6 +37,7 @@ _SIGNATURES = {
     "ozk_stats_rows": ([P, I32, I32, P, P, P, P, P], I32),
     "ozk_stats_cols_workspace_bytes": ([I32, I32], SZ),
     "ozk_stats_cols": ([P, I32, I32, P, P, P, P, P, SZ, P], I32),
+    "ozk_rule_certified": ([P, P, P, I32, I32, I32, P, P, P, P, P], I32),
     "ozk_certificate_workspace_bytes": ([I32, I32, I32], SZ),
     "ozk_certificate": ([P, P, I32, I32, I32, P, P, P, P, P, F64, F64, P, P, P, P, P, SZ, P], I32),
     "ozk_rule_workspace_bytes": ([I32, I32, I32], SZ),

@@ -356,6 +356,39 @@ int probe_blocks(int k) {
 size_t ctl_bytes() { return (sizeof(RuleCtl) + 255) & ~(size_t)255; }
 size_t hard_bytes(int m, int n) { return ((size_t)(m + n) * sizeof(double) + 255) & ~(size_t)255; }
 
+// The rule driven by the full-matrix certificate (min xmax over all entries, csrc/certificate.cu) instead of the
+// probe: p_req = ceil(-log2(xmin) + 1e-9) clamped to [1, 1000] as the sampled rule clamps it, N = the smallest plane
+// count in [6, 32] whose pmax_bits reaches p_req; fallback on non-finite input, no such N, or p_req > 249.
+__global__ void __launch_bounds__(kPrepThreads) rule_certified_kernel(
+    const double* __restrict__ nA, const double* __restrict__ nB, const int32_t* __restrict__ flag, int m, int n, int k,
+    const unsigned long long* __restrict__ xmin, MTable mt, int32_t* __restrict__ dec, int32_t* __restrict__ p_dev,
+    double* __restrict__ aux) {
+    __shared__ double smv[32];
+    __shared__ int pv[OZK_NMAX + 1];
+    double mA = 0.0, mB = 0.0;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) mA = fmax(mA, nA[i]);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) mB = fmax(mB, nB[j]);
+    mA = block_max(mA, smv);
+    mB = block_max(mB, smv);
+    const double nuA = __dsqrt_rn(mA), nuB = __dsqrt_rn(mB);
+    if (threadIdx.x >= 1 && threadIdx.x <= OZK_NMAX) pv[threadIdx.x] = pmax_bits_dev(mt.M[threadIdx.x], nuA, nuB, k);
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    const unsigned long long xb = *xmin;
+    const double need = xb == ~0ULL ? -1e30 : -log2(__longlong_as_double((long long)xb));
+    double pr = ceil(__dadd_rn(need, 1e-9));
+    pr = pr < 1.0 ? 1.0 : (pr > 1000.0 ? 1000.0 : pr);
+    const int preq = (int)pr;
+    int N = 0;
+    for (int t = 6; t <= OZK_NMAX && !N; t++)
+        if (pv[t] >= preq) N = t;
+    const int fb = (flag[0] != 0 || N == 0 || preq > 249) ? 1 : 0;
+    const int p = N ? pv[N] : 0;
+    dec[0] = fb ? 0 : N; dec[1] = p; dec[2] = fb; dec[3] = preq;
+    *p_dev = p;
+    aux[0] = nuA; aux[1] = nuB; aux[2] = need; aux[3] = 0.0; aux[4] = 0.0; aux[5] = 0.0; aux[6] = 0.0; aux[7] = 0.0;
+}
+
 }  // namespace
 
 extern "C" size_t ozk_rule_workspace_bytes(int m, int n, int k) {
@@ -435,4 +468,18 @@ extern "C" int ozk_rule(const double* A, const double* B, int m, int n, int k, c
     if (rc != OZK_OK) return rc;
     if ((rc = ozk_rule_probe(A, B, 0, m, m, n, k, workspace, workspace_bytes, stream)) != OZK_OK) return rc;
     return ozk_rule_finish(r, c, sA, sB, m, n, k, tau, safety, dec, p_dev, aux, workspace, workspace_bytes, stream);
+}
+
+extern "C" int ozk_rule_certified(const double* nA, const double* nB, const int32_t* flag, int m, int n, int k,
+                                  const double* xmin, int32_t* dec, int32_t* p_dev, double* aux, ozk_stream_t stream_) {
+    if (!nA || !nB || !flag || !xmin || !dec || !p_dev || !aux) return OZK_ERR_ARG;
+    if (m <= 0 || n <= 0 || k <= 0) return OZK_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    MTable mt;
+    for (int N = 0; N <= OZK_NMAX; N++) mt.M[N] = N ? ozk_modulus_product(N) : 1.0;
+    rule_certified_kernel<<<1, kPrepThreads, 0, st>>>(nA, nB, flag, m, n, k,
+                                                      reinterpret_cast<const unsigned long long*>(xmin), mt, dec,
+                                                      p_dev, aux);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
 }

@@ -147,6 +147,23 @@ class OzakiCRT:
         self.stats(A, B, b, inside)
         self._rule_device(A, B, b, tau, safety, force_N, force_p, seed=0)
 
+    def _rule_certified(self, A, B, b, tau, safety):
+        """The rule from the full-matrix certificate instead of the probe: one FP16 tensor-core product bounds D on
+        every entry (csrc/certificate.cu), then N, p on the device (``ozk_rule_certified``)."""
+        from .certificate import certificate_device
+        m, k = A.shape
+        n = B.shape[1]
+        w = certificate_device(self, A, B, b["gam"], b["r"], b["c"], b["sA"], b["sB"], tau, safety)
+        check(self.lib.ozk_rule_certified(ptr(b["nA"]), ptr(b["nB"]), ptr(b["flag"]), m, n, k, ptr(w["xmin"]),
+                                          ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]), _stream_handle()),
+              "ozk_rule_certified")
+        self.launches += 1
+        return w
+
+    def _stats_rule_certified(self, A, B, b, tau, safety, inside):
+        self.stats(A, B, b, inside)
+        self._rule_certified(A, B, b, tau, safety)
+
     def _read_ctl(self, b):
         b["hctl"].copy_(b["ctl"], non_blocking=True)
         b["haux"].copy_(b["aux"], non_blocking=True)
@@ -252,19 +269,28 @@ class OzakiCRT:
         g.replay()
         self.launches += 4
 
-    def run_fast(self, A, B, C, tau=2.0 ** -52, safety=2.0, inside=True, force_N=None, force_p=None, events=None):
+    def run_fast(self, A, B, C, tau=2.0 ** -52, safety=2.0, inside=True, force_N=None, force_p=None, events=None,
+                 certify=False):
         """Timed path: [graph: statistics + rule] -> one host read of (N, p) -> [graph: residues, products, recon].
-        ``events`` (a list) receives (name, CUDA event) marks after each part, for stage timing inside a run."""
+        ``events`` (a list) receives (name, CUDA event) marks after each part, for stage timing inside a run.
+        ``certify``: the rule is the full-matrix certificate (every entry) instead of the 96 x 96 probe."""
         self._shape_check(A, B, C)
         m, k = A.shape
         n = B.shape[1]
         if force_N is not None and force_p is not None:
             return self._run_config(A, B, C, tau, safety, inside, int(force_N), int(force_p), events)
+        if certify:
+            force_N = force_p = None
         b = self.buffers(m, n, k, 20)
-        key = ("sr", m, n, k, A.data_ptr(), B.data_ptr(), tau, safety, inside, force_N, force_p)
+        key = ("sr", m, n, k, A.data_ptr(), B.data_ptr(), tau, safety, inside, force_N, force_p, bool(certify))
+
+        def stats_rule(bb):
+            if certify:
+                return lambda: self._stats_rule_certified(A, B, bb, tau, safety, inside)
+            return lambda: self._stats_rule(A, B, bb, tau, safety, inside, force_N, force_p)
         g = self.graphs.get(key)
         if g is None:
-            g = self._capture(lambda: self._stats_rule(A, B, b, tau, safety, inside, force_N, force_p))
+            g = self._capture(stats_rule(b))
             self.graphs[key] = g
 
         def mark(name):
@@ -284,14 +310,17 @@ class OzakiCRT:
             return C, {"fallback": True, "preq": preq}
         if b["N"] < N:
             b = self.buffers(m, n, k, N)
-            g = self._capture(lambda: self._stats_rule(A, B, b, tau, safety, inside, force_N, force_p))
+            g = self._capture(stats_rule(b))
             self.graphs[key] = g
             g.replay()
             ctl, _ = self._read_ctl(b)
             N, p = ctl[0], ctl[1]
         self.core_graph(A, B, b, N, C)
         mark("core")
-        return C, {"N": N, "p": p, "preq": preq}
+        out = {"N": N, "p": p, "preq": preq}
+        if certify:
+            out["certified"] = True
+        return C, out
 
     def _run_config(self, A, B, C, tau, safety, inside, N, p, events=None):
         """Configuration-table fast path (N and p both given, e.g. by pick_config): ONE graph of statistics, the
@@ -336,10 +365,39 @@ class OzakiCRT:
             return C, {"fallback": True, "preq": preq}
         return C, {"N": Nd, "p": pd, "preq": preq}
 
+    def _run_certified(self, A, B, C, tau, inside, safety=2.0):
+        m, k = A.shape
+        n = B.shape[1]
+        b = self.buffers(m, n, k, 20)
+        if C is None:
+            C = torch.empty(m, n, dtype=torch.float64, device=DEV)
+        self.stats(A, B, b, inside)
+        w = self._rule_certified(A, B, b, tau, safety)
+        ctl, aux = self._read_ctl(b)
+        if int(w["err"].item()):
+            raise _lib.OzkError(f"ozk_certificate: device error flag {int(w['err'].item()):#x} (a bounded wait ran out)")
+        h, nonfinite = self.host_stats(b, m, n)
+        info = {"nonfinite": nonfinite, "certified": True, "nuA": aux[0], "nuB": aux[1], "p_req": ctl[3],
+                "uncertified_entries": int(w["unc"].item())}
+        N, p, fb = ctl[0], ctl[1], ctl[2]
+        if fb or N == 0:
+            info["fallback"] = True
+            torch.matmul(A, B, out=C)
+            return C, info
+        if b["N"] < N:
+            b = self.buffers(m, n, k, N)
+            self.stats(A, B, b, inside)
+        b["pdev"].fill_(p)
+        info.update({"N": N, "p": p, "L": limbs_for(N), "stats": h})
+        self.core(A, B, b, N, C)
+        return C, info
+
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, graph=False, prof=None, seed=0, config=None,
-            force_p=None):
+            force_p=None, certify=False):
         """C = A B in emulated FP64; returns (C, info).  ``config`` ({'N':.., 'p':..}, e.g. from pick_config) overrides
-        the a-priori rule (ozaki_engine.py:1460-1505)."""
+        the a-priori rule (ozaki_engine.py:1460-1505).  ``certify=True`` (not in the reference's run) replaces the
+        sampled probe by the full-matrix certificate of every entry (see certificate.py); info then carries
+        ``certified``, ``p_req`` (the certificate's) and ``uncertified_entries``."""
         if config is not None:
             force_N, force_p = int(config["N"]), config.get("p")
         self._shape_check(A, B, C)
@@ -348,7 +406,9 @@ class OzakiCRT:
         if graph:
             if C is None:
                 C = torch.empty(m, n, dtype=torch.float64, device=DEV)
-            return self.run_fast(A, B, C, tau=tau, inside=inside, force_N=force_N, force_p=force_p)
+            return self.run_fast(A, B, C, tau=tau, inside=inside, force_N=force_N, force_p=force_p, certify=certify)
+        if certify and force_N is None:
+            return self._run_certified(A, B, C, tau, inside)
         b = self.buffers(m, n, k, force_N or 20)
         if C is None:
             C = torch.empty(m, n, dtype=torch.float64, device=DEV)

@@ -86,3 +86,28 @@ def test_full_certificate_api(pkg, oracle, engine):
     assert Nf is not None and pkg.pmax_bits(Nf, info["nuA"], info["nuB"], k) >= cert["preq_full"]
     assert Nf == 6 or pkg.pmax_bits(Nf - 1, info["nuA"], info["nuB"], k) < cert["preq_full"]
     assert cert["sampled_config_fully_certified"] == (info["N"] >= Nf)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,k,n,phi", [(256, 1024, 256, 2.0), (128, 512, 384, 0.5)])
+def test_run_certified(pkg, oracle, engine, m, k, n, phi):
+    """The certified rule in the timed path: N from the certificate of every entry, core bit-exact."""
+    import torch
+    A, B = pkg.make_inputs(m, k, n, phi, seed=k + n)
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    C, info = engine.run(Ad, Bd, certify=True)
+    assert info["certified"] and not info.get("fallback")
+    st = oracle.stats(A, B, True)
+    ref = oracle.full_certificate(A, B, st)
+    assert abs(info["p_req"] - ref["preq"]) <= 1
+    N, p = info["N"], info["p"]
+    assert p == oracle.pmax_bits(N, info["nuA"], info["nuB"], k) >= info["p_req"]
+    assert N == 6 or oracle.pmax_bits(N - 1, info["nuA"], info["nuB"], k) < info["p_req"]
+    assert np.array_equal(C.cpu().numpy(), oracle.core(A, B, st, N, p))
+    _, sampled = engine.run(Ad, Bd)
+    assert N >= sampled["N"] - 1                              # the certificate covers the probe entries too
+    Cg = torch.empty_like(C)
+    for _ in range(2):
+        _, ig = engine.run(Ad, Bd, Cg, graph=True, certify=True)
+        assert (ig["N"], ig["p"], ig["preq"]) == (N, p, info["p_req"]) and ig["certified"]
+        assert torch.equal(Cg, C)
