@@ -48,6 +48,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-accuracy", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=0, help="rows = cols of the CPU sample block (0: auto)")
+    ap.add_argument("--mode", default="sampled", choices=["sampled", "certified", "config", "persist"],
+                    help="sampled: the reference's timed path (default); certified: the plane count from the "
+                         "full-matrix certificate; config: the single-graph path with (N, p) given (the sampled "
+                         "rule's choice); persist: PersistA, A encoded once per step and --q products")
+    ap.add_argument("--q", type=int, default=4, help="products per step in --mode persist")
     return ap.parse_args()
 
 
@@ -234,12 +239,29 @@ def main():
     t_gen = time.perf_counter() - t_gen
 
     step_events = []
+    products = 1
     if world > 1:
+        assert args.mode == "sampled", "--mode other than sampled is single-GPU"
         E = pkg.DistributedOzakiCRT()
         call = lambda ev=None: E.run(A, B, C, force_N=forceN)  # noqa: E731
     else:
         E = pkg.OzakiCRT()
         call = lambda ev=None: E.run_fast(A, B, C, force_N=forceN, events=ev)  # noqa: E731
+        if args.mode == "certified":
+            call = lambda ev=None: E.run_fast(A, B, C, events=ev, certify=True)  # noqa: E731
+        elif args.mode == "config":
+            _, i0 = E.run_fast(A, B, C, force_N=forceN)
+            cfg_N, cfg_p = i0["N"], i0["p"]
+            call = lambda ev=None: E.run_fast(A, B, C, force_N=cfg_N, force_p=cfg_p, events=ev)  # noqa: E731
+        elif args.mode == "persist":
+            PA = pkg.PersistA(E, A, B, n)
+            products = args.q
+
+            def call(ev=None):
+                PA.encode()
+                for _ in range(args.q):
+                    PA.product(B, C)
+                return C, {"N": PA.N, "p": PA.p}
 
     for _ in range(args.warmup):
         _, info = call()
@@ -271,7 +293,7 @@ def main():
         tt = torch.tensor([t_dev], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_dev = float(tt.item())
-    flops = 2.0 * m * n * k
+    flops = 2.0 * m * n * k * products
     value = flops / t_dev / 1e12
 
     # stage times inside the timed calls (CUDA events between the parts of run_fast)
@@ -351,11 +373,13 @@ def main():
     if world > 1:
         dist.barrier()
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+        metric = METRIC if args.mode == "sampled" else METRIC + f" [{args.mode} mode]"
+        line = {"metric": metric, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": t_dev * 1e3, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f64 (int8 residue arithmetic)", "data": "synthetic",
                 "config": {"workload": args.workload, "desc": desc, "m": m, "n": n, "k": k, "phi": phi,
-                           "planes": Nplanes, "p": info.get("p"), "parallelism": f"C row blocks x{world}" if world > 1 else "single GPU",
+                           "planes": Nplanes, "p": info.get("p"), "mode": args.mode, "products_per_step": products,
+                           "parallelism": f"C row blocks x{world}" if world > 1 else "single GPU",
                            "l2": "inputs larger than L2 (2 x 2.1 GB fp64)", "input_generation_s": t_gen},
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "accuracy": acc, "clocks": clocks.summary(),
                 "gpu_launches": launches, "hbm_peak_gbs": hbm_peak, "peaks": peak_src}

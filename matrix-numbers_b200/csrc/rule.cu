@@ -71,50 +71,78 @@ __device__ __forceinline__ double hard_value(int e, double s, int k) {
     return s > 0.0 ? __ddiv_rn(__dmul_rn(ldexp(1.0, e), (double)k), s) : 0.0;
 }
 
-// (v, i) precedes (bv, bi) in the order "larger value first, then lower index" (a stable descending sort)
-__device__ __forceinline__ bool before(double v, int i, double bv, int bi) {
-    return v > bv || (v == bv && i < bi);
+// Select the `cnt` (<= 32) first indices of the stable descending order of the values hv[0..len) ("larger value
+// first, then lower index"); writes them to out[0..cnt).  The values are hard values (>= 0, +inf possible, never
+// NaN), so their bit patterns order like the values.  Each warp keeps the sorted top-32 of its contiguous segment,
+// one entry per lane (a 32-element bitonic sort per chunk of 32, then a bitonic merge with the running list); the 32
+// lists are merged pairwise in 5 rounds through shared memory.  Ties between values are broken by index, so the
+// result is the same set and order as a stable sort.
+struct KeyIdx { unsigned long long key; int idx; };
+
+__device__ __forceinline__ bool kbefore(unsigned long long k, int i, unsigned long long bk, int bi) {
+    return k > bk || (k == bk && i < bi);
 }
 
-// Select the `cnt` first indices of the stable descending order of the values hv[0..len); writes them to out[0..cnt).
-__device__ void top_hard(const double* __restrict__ hv, int len, int cnt, int* out, double* smv, int* smi) {
-    double pv = INFINITY;
-    int pi = -1;
-    for (int round = 0; round < cnt; round++) {
-        double bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int x = threadIdx.x; x < len; x += blockDim.x) {
-            const double v = hv[x];
-            const bool after_prev = (v < pv) || (v == pv && x > pi);
-            if (after_prev && before(v, x, bv, bi)) { bv = v; bi = x; }
-        }
-        // block argmax in the same order
-        for (int o = 16; o > 0; o >>= 1) {
-            const double ov = __shfl_down_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_down_sync(0xffffffffu, bi, o);
-            if (before(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-        }
-        const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
-        __syncthreads();
-        if (ln == 0) { smv[w] = bv; smi[w] = bi; }
-        __syncthreads();
-        if (w == 0) {
-            bv = ln < (int)(blockDim.x >> 5) ? smv[ln] : -INFINITY;
-            bi = ln < (int)(blockDim.x >> 5) ? smi[ln] : 0x7fffffff;
-            for (int o = 16; o > 0; o >>= 1) {
-                const double ov = __shfl_down_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_down_sync(0xffffffffu, bi, o);
-                if (before(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-            }
-            if (ln == 0) { smv[0] = bv; smi[0] = bi; }
-        }
-        __syncthreads();
-        pv = smv[0];
-        pi = smi[0];
-        __syncthreads();
-        if (pi == 0x7fffffff) pi = 0;   // only non-comparable (NaN) values left: fall back to index 0
-        if (threadIdx.x == 0) out[round] = pi;
+__device__ __forceinline__ void cswap_lane(unsigned long long& key, int& idx, int j, bool keep_better) {
+    const unsigned long long pk = __shfl_xor_sync(0xffffffffu, key, j);
+    const int pi = __shfl_xor_sync(0xffffffffu, idx, j);
+    const bool take = keep_better ? kbefore(pk, pi, key, idx) : kbefore(key, idx, pk, pi);
+    if (take) { key = pk; idx = pi; }
+}
+
+// lanes hold a bitonic sequence; leaves it sorted best-first
+__device__ __forceinline__ void bitonic_merge_desc(unsigned long long& key, int& idx) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) cswap_lane(key, idx, j, (lane & j) == 0);
+}
+
+__device__ __forceinline__ void bitonic_sort_desc(unsigned long long& key, int& idx) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) cswap_lane(key, idx, j, (((lane & k) == 0) == ((lane & j) == 0)));
+}
+
+// merge the other sorted list (ok, oi: entry `lane` of it) into this one; keeps the best 32, sorted
+__device__ __forceinline__ void merge_lists(unsigned long long& key, int& idx, unsigned long long ok, int oi) {
+    const int lane = threadIdx.x & 31;
+    const unsigned long long rk = __shfl_sync(0xffffffffu, ok, 31 - lane);
+    const int ri = __shfl_sync(0xffffffffu, oi, 31 - lane);
+    if (kbefore(rk, ri, key, idx)) { key = rk; idx = ri; }
+    bitonic_merge_desc(key, idx);
+}
+
+constexpr int kNoIdx = 0x7fffffff;
+
+__device__ void top_hard(const double* __restrict__ hv, int len, int cnt, int* out, KeyIdx* lists) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int seg = (len + nw - 1) / nw;
+    const int b0 = w * seg, b1 = min(len, b0 + seg);
+    unsigned long long key = 0ULL;
+    int idx = kNoIdx;
+    for (int c0 = b0; c0 < b1; c0 += 32) {
+        const int x = c0 + lane;
+        unsigned long long ck = 0ULL;
+        int ci = kNoIdx;
+        if (x < b1) { ck = (unsigned long long)__double_as_longlong(hv[x]); ci = x; }
+        bitonic_sort_desc(ck, ci);
+        merge_lists(key, idx, ck, ci);
     }
+    lists[w * 32 + lane] = KeyIdx{key, idx};
+    __syncthreads();
+    for (int half = nw >> 1; half > 0; half >>= 1) {
+        if (w < half) {
+            const KeyIdx o = lists[(w + half) * 32 + lane];
+            merge_lists(key, idx, o.key, o.idx);
+        }
+        __syncthreads();
+        if (w < half) lists[w * 32 + lane] = KeyIdx{key, idx};
+        __syncthreads();
+    }
+    if (w == 0 && lane < cnt) out[lane] = idx == kNoIdx ? 0 : idx;
+    __syncthreads();
 }
 
 __device__ double block_max(double v, double* sm) {
@@ -140,7 +168,6 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
     int m, int n, int k, int force_N, int force_p, MTable mt, RuleCtl* __restrict__ ctl, int32_t* __restrict__ dec,
     int32_t* __restrict__ p_dev, double* __restrict__ aux, double* __restrict__ hv) {
     __shared__ double smv[32];
-    __shared__ int smi[32];
     // max nA, max nB (order-independent)
     double mA = 0.0, mB = 0.0;
     for (int i = threadIdx.x; i < m; i += blockDim.x) mA = fmax(mA, nA[i]);
@@ -179,8 +206,9 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
     for (int x = threadIdx.x; x < m; x += blockDim.x) hv[x] = hard_value(r[x], sA[x], k);
     for (int x = threadIdx.x; x < n; x += blockDim.x) hv[m + x] = hard_value(c[x], sB[x], k);
     __syncthreads();
-    top_hard(hv, m, hr, ctl->I + nIr, smv, smi);
-    top_hard(hv + m, n, hc, ctl->J + nJr, smv, smi);
+    __shared__ KeyIdx lists[kPrepThreads];
+    top_hard(hv, m, hr, ctl->I + nIr, lists);
+    top_hard(hv + m, n, hc, ctl->J + nJr, lists);
 }
 
 // split-K probe product: partial[b][a][j] = sum over this block's contraction tiles of |A_I[a] l| |B_l J[j]|
@@ -329,20 +357,27 @@ __global__ void __launch_bounds__(kFinalThreads) rule_final_kernel(
         const int fb = N == 0;
         dec[0] = N; dec[1] = p; dec[2] = fb; dec[3] = preq;
         *p_dev = p;
-        int du = 0, dv = 0;
-        for (int a = 0; a < nI; a++) {
-            bool seen = false;
-            for (int b = 0; b < a; b++) seen |= ctl->I[b] == ctl->I[a];
-            du += !seen;
-        }
-        for (int a = 0; a < nJ; a++) {
-            bool seen = false;
-            for (int b = 0; b < a; b++) seen |= ctl->J[b] == ctl->J[a];
-            dv += !seen;
-        }
-        aux[0] = ctl->nuA; aux[1] = ctl->nuB; aux[2] = w; aux[3] = (double)du; aux[4] = (double)dv;
+        aux[0] = ctl->nuA; aux[1] = ctl->nuB; aux[2] = w;
         aux[5] = 0.0; aux[6] = 0.0; aux[7] = 0.0;
     }
+    // distinct probe rows and columns (the reference reports len(set(I)), len(set(J))): an index counts when no
+    // earlier entry holds it; one thread per entry
+    __shared__ int s_du, s_dv;
+    if (threadIdx.x == 0) { s_du = 0; s_dv = 0; }
+    __syncthreads();
+    if (threadIdx.x < nI) {
+        const int a = threadIdx.x, v = ctl->I[a];
+        bool seen = false;
+        for (int b = 0; b < a; b++) seen |= ctl->I[b] == v;
+        if (!seen) atomicAdd(&s_du, 1);
+    } else if (threadIdx.x >= 512 && threadIdx.x - 512 < nJ) {
+        const int a = threadIdx.x - 512, v = ctl->J[a];
+        bool seen = false;
+        for (int b = 0; b < a; b++) seen |= ctl->J[b] == v;
+        if (!seen) atomicAdd(&s_dv, 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { aux[3] = (double)s_du; aux[4] = (double)s_dv; }
 }
 
 int probe_blocks(int k) {

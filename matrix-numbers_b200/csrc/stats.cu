@@ -12,7 +12,15 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kColmaxRows = 64;     // rows of A folded by one block of colmax_a_kernel
-constexpr int kColChunk = 512;      // rows of B folded by one block of the column kernels
+// rows of B folded by one block of the column kernels: at most 512, fewer when B has few columns, so that the grid
+// keeps about 600 blocks (a function of n and k only: the workspace size depends on it)
+__host__ __device__ inline int col_chunk_rows(int n, int k) {
+    const int colblocks = (n / 2 + 255) / 256;
+    const int want = (600 + colblocks - 1) / colblocks;
+    int rows = (k + want - 1) / want;
+    rows = (rows + 7) & ~7;
+    return rows < 8 ? 8 : (rows > 512 ? 512 : rows);
+}
 
 template <typename T, typename Op>
 __device__ __forceinline__ T block_reduce(T v, T identity, T* sm, Op op) {
@@ -148,14 +156,14 @@ __global__ void __launch_bounds__(kThreads) rowstats_a_kernel(const double* __re
     if (threadIdx.x == 0) { r_out[i] = rr; s_out[i] = s; n_out[i] = qq; }
 }
 
-// column statistics of B over one chunk of kColChunk rows, 2 columns per thread, one pass (colexpB_k and colsumsB_k,
+// column statistics of B over one chunk of `chunk` rows, 2 columns per thread, one pass (colexpB_k and colsumsB_k,
 // :926-951): per chunk the local maximum exponent, sB partial and nB partial relative to the local maximum
 __global__ void __launch_bounds__(kThreads) colstats_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ gam,
-                                                              int k, int n, int32_t* __restrict__ pc,
+                                                              int k, int n, int chunk, int32_t* __restrict__ pc,
                                                               double* __restrict__ ps, double* __restrict__ pq) {
     const int j = 2 * (blockIdx.x * kThreads + threadIdx.x);
     if (j >= n) return;
-    const int l0 = blockIdx.y * kColChunk, l1 = min(k, l0 + kColChunk);
+    const int l0 = blockIdx.y * chunk, l1 = min(k, l0 + chunk);
     RunStats r0, r1;
     r0.init();
     r1.init();
@@ -198,7 +206,7 @@ static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 extern "C" size_t ozk_stats_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
-    const size_t nchunks = ((size_t)k + kColChunk - 1) / kColChunk;
+    const size_t nchunks = ((size_t)k + col_chunk_rows(n, k) - 1) / col_chunk_rows(n, k);
     return align256((size_t)k * 8) * 2 + align256(nchunks * (size_t)n * 8) * 2 + align256(nchunks * (size_t)n * 4);
 }
 
@@ -222,7 +230,8 @@ extern "C" int ozk_stats_finish(const double* A, const double* B, int m, int n, 
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return OZK_ERR_ARG;
     if (workspace_bytes < ozk_stats_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
-    const int nchunks = (k + kColChunk - 1) / kColChunk;
+    const int chunk = col_chunk_rows(n, k);
+    const int nchunks = (k + chunk - 1) / chunk;
     char* ws = static_cast<char*>(workspace);
     unsigned long long* rowmax = reinterpret_cast<unsigned long long*>(ws + align256((size_t)k * 8));
     double* ps = reinterpret_cast<double*>(ws + 2 * align256((size_t)k * 8));
@@ -237,7 +246,7 @@ extern "C" int ozk_stats_finish(const double* A, const double* B, int m, int n, 
     OZK_CHECK_LAUNCH();
     int32_t* pc = reinterpret_cast<int32_t*>(ws + 2 * align256((size_t)k * 8) + 2 * align256((size_t)nchunks * n * 8));
     const dim3 g2((n / 2 + kThreads - 1) / kThreads, nchunks);
-    colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, pc, ps, pq);
+    colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, chunk, pc, ps, pq);
     OZK_CHECK_LAUNCH();
     colstats_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
     OZK_CHECK_LAUNCH();
@@ -257,7 +266,7 @@ extern "C" int ozk_stats_rows(const double* A, int m, int k, const int32_t* gam,
 
 extern "C" size_t ozk_stats_cols_workspace_bytes(int k, int n) {
     if (n <= 0 || k <= 0) return 0;
-    const size_t nchunks = ((size_t)k + kColChunk - 1) / kColChunk;
+    const size_t nchunks = ((size_t)k + col_chunk_rows(n, k) - 1) / col_chunk_rows(n, k);
     return align256(nchunks * (size_t)n * 8) * 2 + align256(nchunks * (size_t)n * 4);
 }
 
@@ -268,13 +277,14 @@ extern "C" int ozk_stats_cols(const double* B, int k, int n, const int32_t* gam,
     if (reinterpret_cast<uintptr_t>(B) & 15) return OZK_ERR_ARG;
     if (workspace_bytes < ozk_stats_cols_workspace_bytes(k, n)) return OZK_ERR_WORKSPACE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
-    const int nchunks = (k + kColChunk - 1) / kColChunk;
+    const int chunk = col_chunk_rows(n, k);
+    const int nchunks = (k + chunk - 1) / chunk;
     char* ws = static_cast<char*>(workspace);
     double* ps = reinterpret_cast<double*>(ws);
     double* pq = reinterpret_cast<double*>(ws + align256((size_t)nchunks * n * 8));
     int32_t* pc = reinterpret_cast<int32_t*>(ws + 2 * align256((size_t)nchunks * n * 8));
     const dim3 g2((n / 2 + kThreads - 1) / kThreads, nchunks);
-    colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, pc, ps, pq);
+    colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, chunk, pc, ps, pq);
     OZK_CHECK_LAUNCH();
     colstats_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
     OZK_CHECK_LAUNCH();

@@ -461,3 +461,40 @@ def test_accuracy_lemma_L1_and_native(pkg, engine, torch_mod):
     err = np.abs(Cs - S.ref)
     lim = Eb * (1 + 1e-9) + 2.0 ** -53 * (np.abs(Cs) + np.abs(S.ref)) * (1 + 1e-9)
     assert int((err > lim).sum()) == 0
+
+
+# the hard-row / hard-column selection of the rule (top 32 of 2^r k / s, stable: larger first, then lower index),
+# read back from the rule workspace (RuleCtl: done, nI, nJ, pad, pv[33], nuA, nuB, I[96] at byte 168, J[96] at 552)
+@pytest.mark.parametrize("m,n,ties", [(1000, 64, True), (4096, 2048, False), (20, 40, True), (33000, 96, True)])
+def test_rule_hard_selection(pkg, oracle, torch_mod, m, n, ties):
+    torch = torch_mod
+    L = pkg._lib.lib()
+    ptr = pkg._lib.ptr
+    rng = np.random.default_rng(m)
+    k = 512
+    if ties:   # few distinct values: long runs of equal hard values
+        r = rng.integers(-3, 3, m).astype(np.int32)
+        sA = rng.choice([1.0, 2.0, 4.0], m)
+        c = rng.integers(-3, 3, n).astype(np.int32)
+        sB = rng.choice([1.0, 2.0], n)
+    else:
+        r = rng.integers(-40, 40, m).astype(np.int32)
+        sA = rng.uniform(0.5, 600.0, m)
+        c = rng.integers(-40, 40, n).astype(np.int32)
+        sB = rng.uniform(0.5, 600.0, n)
+    sA[::7] = 0.0                                           # hard value 0
+    dv = {x: torch.from_numpy(np.ascontiguousarray(v)).cuda() for x, v in
+          (("r", r), ("c", c), ("sA", sA), ("sB", sB), ("nA", np.ones(m)), ("nB", np.ones(n)),
+           ("flag", np.zeros(1, np.int32)))}
+    ws = torch.zeros(L.ozk_rule_workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    ctl = torch.zeros(8, dtype=torch.int32, device="cuda")
+    aux = torch.zeros(8, dtype=torch.float64, device="cuda")
+    pkg._lib.check(L.ozk_rule_prepare(ptr(dv["r"]), ptr(dv["c"]), ptr(dv["sA"]), ptr(dv["nA"]), ptr(dv["sB"]),
+                                      ptr(dv["nB"]), ptr(dv["flag"]), m, n, k, None, 0, None, 0, 0, -1,
+                                      ptr(ctl[0:4]), ptr(ctl[5:6]), ptr(aux), ptr(ws), ws.numel(),
+                                      torch.cuda.current_stream().cuda_stream), "ozk_rule_prepare")
+    torch.cuda.synchronize()
+    raw = ws.cpu().numpy()
+    I = raw[168:168 + 96 * 4].view(np.int32)[:min(32, m)]
+    J = raw[552:552 + 96 * 4].view(np.int32)[:min(32, n)]
+    assert np.array_equal(I, oracle.hard_top(r, sA, k)) and np.array_equal(J, oracle.hard_top(c, sB, k))
