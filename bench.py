@@ -6,8 +6,8 @@
 One step = one call of the drop-in entry point ``OzakiCRT.run(A, B, C, graph=True)`` (statistics, the device rule,
 the host read of (N, p), residue split, the N INT8 tensor-core products with the fused reduction, reconstruction)
 on inputs resident in HBM.  Default workload: the metric's n = 16384 configuration (c3: M = N = K = 16384, entries
-(U - 0.5) exp(2 N(0,1)), seed 0, dynamic plane rule).  With --gpus N > 1 the same product is split into C row
-blocks, one per rank (DistributedOzakiCRT; strong scaling).
+(U - 0.5) exp(2 N(0,1)), seed 0, dynamic plane rule).  With --gpus N > 1 the same product is split into an R x S
+grid of C blocks, one per rank (DistributedOzakiCRT: S = 2 from 4 ranks on, else row blocks; strong scaling).
 
 Printed (rank 0, one JSON line): value (device time, max over ranks), e2e (the same call from pinned host buffers,
 H2D + D2H inside the timed region), roofline of the INT8 product kernel (live CUDA-event time of its launches), the
@@ -227,22 +227,28 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     m, k, n, phi, alt, forceN, desc = pkg.CONFIGS[args.workload]
 
-    # inputs: generated on the host (numpy, seed 0), A's row block per rank, B on every rank
+    # inputs: generated on the host (numpy, seed 0); rank a S + b of the R x S grid holds A's row block a and B's
+    # column block b (R = world, S = 1 for a plain row split)
     t_gen = time.perf_counter()
     A_host, B_host = pkg.make_inputs(m, k, n, phi, 0, alt)
-    rows = m // world
-    assert rows % 4 == 0, "rows per rank must be a multiple of 4"
-    r0 = rank * rows
-    A = torch.from_numpy(A_host[r0:r0 + rows]).to(dev)
-    B = torch.from_numpy(B_host).to(dev)
-    C = torch.empty((rows, n), dtype=torch.float64, device=dev)
+    from matrix_numbers_b200.distributed import default_grid
+    R, S = default_grid(world) if world > 1 else (1, 1)
+    ga, gb = divmod(rank, S)
+    rows, cols = m // R, n // S
+    assert rows % 4 == 0 and cols % 32 == 0, "block shape rule"
+    r0, c0 = ga * rows, gb * cols
+    A_blk = A_host[r0:r0 + rows]
+    B_blk = np.ascontiguousarray(B_host[:, c0:c0 + cols]) if S > 1 else B_host
+    A = torch.from_numpy(A_blk).to(dev)
+    B = torch.from_numpy(B_blk).to(dev)
+    C = torch.empty((rows, cols), dtype=torch.float64, device=dev)
     t_gen = time.perf_counter() - t_gen
 
     step_events = []
     products = 1
     if world > 1:
         assert args.mode == "sampled", "--mode other than sampled is single-GPU"
-        E = pkg.DistributedOzakiCRT()
+        E = pkg.DistributedOzakiCRT(grid=(R, S))
         call = lambda ev=None: E.run(A, B, C, force_N=forceN)  # noqa: E731
     else:
         E = pkg.OzakiCRT()
@@ -306,11 +312,11 @@ def main():
     Nplanes = info.get("N") or forceN
     prof = {}
     engine = E.engine if world > 1 else E
-    b = engine.buffers(rows, n, k, Nplanes)
+    b = engine.buffers(rows, cols, k, Nplanes)
     for _ in range(3):
         engine.core(A, B, b, Nplanes, C, prof=prof)
     t_gemm = prof["gemm+reduce"] / 3
-    int8_ops = 2.0 * Nplanes * rows * n * k
+    int8_ops = 2.0 * Nplanes * rows * cols * k
     peak_int8 = int8_peak_tops(torch, dev)
     hbm_peak, bf16_peak, peak_src = measured_peaks()
     achieved = int8_ops / t_gemm / 1e12
@@ -332,16 +338,17 @@ def main():
         t1.record()
         torch.cuda.synchronize()
         t_nat = t0.elapsed_time(t1) / 1e3
-        S = pkg.Sample(A, B, Cn, nr=24, nc=24)
-        acc = {"engine": S.errors(C), "native_dgemm": S.errors(Cn), "native_dgemm_tflops": 2.0 * rows * n * k / t_nat / 1e12}
+        Smp = pkg.Sample(A, B, Cn, nr=24, nc=24)
+        acc = {"engine": Smp.errors(C), "native_dgemm": Smp.errors(Cn),
+               "native_dgemm_tflops": 2.0 * rows * cols * k / t_nat / 1e12}
         del Cn
 
     # end to end through the public API with host buffers (pinned), H2D + D2H inside the timed region
     e2e = None
     if args.e2e_steps > 0:
-        Ah = torch.from_numpy(A_host[r0:r0 + rows]).pin_memory()
-        Bh = torch.from_numpy(B_host).pin_memory()
-        Ch = torch.empty((rows, n), dtype=torch.float64).pin_memory()
+        Ah = torch.from_numpy(A_blk).pin_memory()
+        Bh = torch.from_numpy(B_blk).pin_memory()
+        Ch = torch.empty((rows, cols), dtype=torch.float64).pin_memory()
         call()
         torch.cuda.synchronize()
         if world > 1:
@@ -379,7 +386,7 @@ def main():
                 "vs_baseline": None, "dtype": "f64 (int8 residue arithmetic)", "data": "synthetic",
                 "config": {"workload": args.workload, "desc": desc, "m": m, "n": n, "k": k, "phi": phi,
                            "planes": Nplanes, "p": info.get("p"), "mode": args.mode, "products_per_step": products,
-                           "parallelism": f"C row blocks x{world}" if world > 1 else "single GPU",
+                           "parallelism": f"{R} x {S} grid of C blocks" if world > 1 else "single GPU",
                            "l2": "inputs larger than L2 (2 x 2.1 GB fp64)", "input_generation_s": t_gen},
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "accuracy": acc, "clocks": clocks.summary(),
                 "gpu_launches": launches, "hbm_peak_gbs": hbm_peak, "peaks": peak_src}

@@ -79,6 +79,16 @@ int ozk_stats_finish(const double* A, const double* B, int m, int n, int k, int 
                      int32_t* gam, int32_t* r, int32_t* c, double* sA, double* nA, double* sB, double* nB,
                      int32_t* flag, void* workspace, size_t workspace_bytes, ozk_stream_t stream);
 
+/* Stage 1 in pieces, for a 2-D grid of C blocks over several GPUs (row blocks of A x column blocks of B; the
+ * maxima are all-reduced with MAX between the ranks before gamma):
+ *   ozk_stats_rowmax: rowmax[k] = max_j |B_lj| over this rank's columns (B_cols: k x n, row-major), as IEEE bit
+ *                     patterns (the reference's rowmax_k, :856-868);
+ *   ozk_stats_gamma:  gamma[k] and the non-finite flag from the (global) colmax and rowmax (gamma_k, :870-879);
+ * then ozk_stats_rows / ozk_stats_cols below for this rank's rows of A and columns of B.                    */
+int ozk_stats_rowmax(const double* B_cols, int k, int n, uint64_t* rowmax, ozk_stream_t stream);
+int ozk_stats_gamma(const uint64_t* colmax, const uint64_t* rowmax, int k, int inside, int32_t* gam, int32_t* flag,
+                    ozk_stream_t stream);
+
 /* One operand's statistics for a given gamma[k] (inside scaling already decided), for the persistent fixed
  * operand mode (the reference's PersistA, ozaki_engine.py:2417-2466, which launches rowstatsA_k alone in encode,
  * :2433-2442, and colexpB_k + colsumsB_k alone in _stats_B, :2444-2454, with gamma = 0):
@@ -133,6 +143,11 @@ int ozk_rule_prepare(const int32_t* r, const int32_t* c, const double* sA, const
                      ozk_stream_t stream);
 int ozk_rule_probe(const double* A_rows, const double* B, int row_begin, int rows, int m, int n, int k,
                    void* workspace, size_t workspace_bytes, ozk_stream_t stream);
+/* The probe product for the rows [row_begin, row_begin + rows) of A and the columns [col_begin, col_begin +
+ * cols) of B held by one rank (B_cols: k x cols, row-major); entries outside the block are zero, the callers sum
+ * the D matrices of all blocks.  ozk_rule_probe == ozk_rule_probe_block with the full column range.          */
+int ozk_rule_probe_block(const double* A_rows, const double* B_cols, int row_begin, int rows, int col_begin, int cols,
+                         int m, int n, int k, void* workspace, size_t workspace_bytes, ozk_stream_t stream);
 int ozk_rule_finish(const int32_t* r, const int32_t* c, const double* sA, const double* sB, int m, int n, int k,
                     double tau, double safety, int32_t* dec, int32_t* p_dev, double* aux, void* workspace,
                     size_t workspace_bytes, ozk_stream_t stream);

@@ -35,6 +35,8 @@ _SIGNATURES = {
     "ozk_stats_colmax": ([P, I32, I32, P, P], I32),
     "ozk_stats_finish": ([P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, SZ, P], I32),
     "ozk_stats_rows": ([P, I32, I32, P, P, P, P, P], I32),
+    "ozk_stats_rowmax": ([P, I32, I32, P, P], I32),
+    "ozk_stats_gamma": ([P, P, I32, I32, P, P, P], I32),
     "ozk_stats_cols_workspace_bytes": ([I32, I32], SZ),
     "ozk_stats_cols": ([P, I32, I32, P, P, P, P, P, SZ, P], I32),
     "ozk_rule_certified": ([P, P, P, I32, I32, I32, P, P, P, P, P], I32),
@@ -44,6 +46,7 @@ _SIGNATURES = {
     "ozk_rule_probe_offset": ([I32, I32, I32], SZ),
     "ozk_rule_prepare": ([P, P, P, P, P, P, P, I32, I32, I32, P, I32, P, I32, I32, I32, P, P, P, P, SZ, P], I32),
     "ozk_rule_probe": ([P, P, I32, I32, I32, I32, I32, P, SZ, P], I32),
+    "ozk_rule_probe_block": ([P, P, I32, I32, I32, I32, I32, I32, I32, P, SZ, P], I32),
     "ozk_rule_finish": ([P, P, P, P, I32, I32, I32, F64, F64, P, P, P, P, SZ, P], I32),
     "ozk_rule": ([P, P, I32, I32, I32, P, P, P, P, P, P, P, P, I32, P, I32, F64, F64, I32, I32, P, P, P, P, SZ, P], I32),
     "ozk_split_a": ([P, P, P, P, I32, I32, I32, P, P], I32),

@@ -215,7 +215,8 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
 // A holds rows [row_begin, row_begin + rows) of the full matrix; probe rows outside it contribute zeros (another
 // GPU's block supplies them; the callers sum the D matrices of all blocks)
 __global__ void __launch_bounds__(kProbeThreads) probe_partial_kernel(const double* __restrict__ A, const double* __restrict__ B,
-                                                                      int row_begin, int rows, int n, int k,
+                                                                      int row_begin, int rows, int col_begin, int cols,
+                                                                      int k,
                                                                       const RuleCtl* __restrict__ ctl,
                                                                       double* __restrict__ partial) {
     if (ctl->done) return;
@@ -226,7 +227,8 @@ __global__ void __launch_bounds__(kProbeThreads) probe_partial_kernel(const doub
     for (int x = threadIdx.x; x < kProbeMax; x += blockDim.x) {
         const int gi = x < nI ? ctl->I[x] - row_begin : -1;
         sI[x] = (gi >= 0 && gi < rows) ? gi : -1;
-        sJ[x] = x < nJ ? ctl->J[x] : -1;
+        const int gj = x < nJ ? ctl->J[x] - col_begin : -1;
+        sJ[x] = (gj >= 0 && gj < cols) ? gj : -1;
     }
     const int a0 = (threadIdx.x >> 4) * 6, b0 = (threadIdx.x & 15) * 6;
     double acc[6][6];
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(kProbeThreads) probe_partial_kernel(const doub
         for (int x = threadIdx.x; x < kProbeMax * kProbeK; x += blockDim.x) {
             const int l = x / kProbeMax, b = x % kProbeMax;
             const int col = sJ[b];
-            sb[l][b] = (col >= 0 && l0 + l < k) ? fabs(__ldg(B + (size_t)(l0 + l) * n + col)) : 0.0;
+            sb[l][b] = (col >= 0 && l0 + l < k) ? fabs(__ldg(B + (size_t)(l0 + l) * cols + col)) : 0.0;
         }
         __syncthreads();
 #pragma unroll 4
@@ -461,21 +463,28 @@ extern "C" int ozk_rule_prepare(const int32_t* r, const int32_t* c, const double
     return OZK_OK;
 }
 
-extern "C" int ozk_rule_probe(const double* A_rows, const double* B, int row_begin, int rows, int m, int n, int k,
-                              void* workspace, size_t workspace_bytes, ozk_stream_t stream_) {
-    if (!A_rows || !B || !workspace) return OZK_ERR_ARG;
+extern "C" int ozk_rule_probe_block(const double* A_rows, const double* B_cols, int row_begin, int rows, int col_begin,
+                                    int cols, int m, int n, int k, void* workspace, size_t workspace_bytes,
+                                    ozk_stream_t stream_) {
+    if (!A_rows || !B_cols || !workspace) return OZK_ERR_ARG;
     if (m <= 0 || n <= 0 || k <= 0 || rows <= 0 || row_begin < 0 || row_begin + rows > m) return OZK_ERR_ARG;
+    if (cols <= 0 || col_begin < 0 || col_begin + cols > n) return OZK_ERR_ARG;
     if (workspace_bytes < ozk_rule_workspace_bytes(m, n, k)) return OZK_ERR_WORKSPACE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
     RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
     double* partial = reinterpret_cast<double*>(static_cast<char*>(workspace) + ctl_bytes() + hard_bytes(m, n));
     const int nb = probe_blocks(k);
-    probe_partial_kernel<<<nb, kProbeThreads, 0, st>>>(A_rows, B, row_begin, rows, n, k, ctl, partial);
+    probe_partial_kernel<<<nb, kProbeThreads, 0, st>>>(A_rows, B_cols, row_begin, rows, col_begin, cols, k, ctl, partial);
     OZK_CHECK_LAUNCH();
     double* D = partial + (size_t)nb * kProbeMax * kProbeMax;
     probe_reduce_kernel<<<(kProbeMax * kProbeMax + 255) / 256, 256, 0, st>>>(partial, nb, ctl, D);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
+}
+
+extern "C" int ozk_rule_probe(const double* A_rows, const double* B, int row_begin, int rows, int m, int n, int k,
+                              void* workspace, size_t workspace_bytes, ozk_stream_t stream) {
+    return ozk_rule_probe_block(A_rows, B, row_begin, rows, 0, n, m, n, k, workspace, workspace_bytes, stream);
 }
 
 extern "C" int ozk_rule_finish(const int32_t* r, const int32_t* c, const double* sA, const double* sB, int m, int n,

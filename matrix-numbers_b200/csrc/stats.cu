@@ -253,6 +253,28 @@ extern "C" int ozk_stats_finish(const double* A, const double* B, int m, int n, 
     return OZK_OK;
 }
 
+extern "C" int ozk_stats_rowmax(const double* B, int k, int n, uint64_t* rowmax, ozk_stream_t stream_) {
+    if (!B || !rowmax) return OZK_ERR_ARG;
+    if (n <= 0 || k <= 0 || (n & 1)) return OZK_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(B) & 15) return OZK_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    rowmax_b_kernel<<<k, kThreads, 0, st>>>(B, reinterpret_cast<unsigned long long*>(rowmax), n);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}
+
+extern "C" int ozk_stats_gamma(const uint64_t* colmax, const uint64_t* rowmax, int k, int inside, int32_t* gam,
+                               int32_t* flag, ozk_stream_t stream_) {
+    if (!colmax || !rowmax || !gam || !flag || k <= 0) return OZK_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    if (cudaMemsetAsync(flag, 0, 4, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
+    gamma_kernel<<<(k + 255) / 256, 256, 0, st>>>(reinterpret_cast<const unsigned long long*>(colmax),
+                                                  reinterpret_cast<const unsigned long long*>(rowmax), gam, flag, k,
+                                                  inside ? 1 : 0);
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}
+
 extern "C" int ozk_stats_rows(const double* A, int m, int k, const int32_t* gam, int32_t* r, double* sA, double* nA,
                               ozk_stream_t stream_) {
     if (!A || !gam || !r || !sA || !nA) return OZK_ERR_ARG;

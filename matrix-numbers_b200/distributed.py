@@ -1,18 +1,21 @@
-"""C row-block sharding of the FP64-on-INT8 GEMM over the ranks of a torch.distributed process group.
+"""The FP64-on-INT8 GEMM over the ranks of a torch.distributed process group, as a 2-D grid of C blocks.
 
-The reference engine runs on one GPU only (dl1683/matrix-numbers code/ozaki_engine.py:443, :531).  Output rows are
-independent once the statistics are global, so rank g owns rows [g m/G, (g+1) m/G) of A and C and B is present on
-every rank (or broadcast from one rank first, ``b_root``).  One call makes these collective steps, in this order on
-every rank:
+The reference engine runs on one GPU only (dl1683/matrix-numbers code/ozaki_engine.py:443, :531).  Blocks of C are
+independent once the statistics are global, so the ranks form an R x S grid: rank g = a S + b holds the row block a
+of A (m/R rows, all of k) and the column block b of B (k x n/S, stored contiguously) and computes the block (a, b)
+of C.  S = 1 is the plain row-block split (B on every rank); S > 1 also divides the B-side work (its statistics and
+residue planes), which otherwise every rank would repeat for the whole of B.  One call makes these collective steps,
+in this order on every rank:
 
-  1. all_reduce(MAX) of the per-column max |A| bit patterns (k int64)  -> the global inside scaling gamma;
-  2. all_gather of the row statistics (r, sA, nA; 20 bytes per row)     -> every rank builds the same probe set
-     (64 random rows + the 32 globally hardest rows) and the same nu_A;
-  3. all_reduce(SUM) of the probe product D (96 x 96 doubles; each rank fills the probe rows it owns, zeros elsewhere)
-     -> every rank makes the same decision (N, p) from the same numbers;
-then each rank splits its A rows and B into residue planes, runs the N INT8 products and reconstructs its C rows --
-no further communication.  The result equals the single-GPU product bit for bit (same gamma, r, c, N, p, and the CRT
-stage is exact).
+  1. all_reduce(MAX) of the per-column max |A| and of the per-row max |B| bit patterns (2 x k int64)
+     -> every rank computes the same inside scaling gamma and non-finite flag;
+  2. all_gather of the row statistics (r, sA, nA) and of the column statistics (c, sB, nB)
+     -> every rank builds the same probe set (64 random + the 32 globally hardest rows / columns) and the same nu;
+  3. all_reduce(SUM) of the probe product D (96 x 96 doubles; each rank fills the entries whose probe row and probe
+     column it holds, zeros elsewhere) -> every rank makes the same decision (N, p) from the same numbers;
+then each rank splits its A rows and B columns into residue planes, runs the N INT8 products and reconstructs its C
+block -- no further communication.  The result equals the single-GPU product bit for bit (same gamma, r, c, N, p;
+the CRT stage is exact).
 
 Compute is delegated to an ``ops`` object: ``CudaOps`` (default) calls libozaki_b200.so on the rank's GPU; the CPU
 tests substitute an implementation with the same interface to check the orchestration over gloo ranks.
@@ -27,6 +30,13 @@ from . import _lib
 from ._lib import check, ptr
 
 
+def default_grid(world: int):
+    """R x S with S = 2 from 4 ranks on (the B-side work halves), else a plain row split."""
+    if world >= 4 and world % 2 == 0:
+        return world // 2, 2
+    return world, 1
+
+
 class CudaOps:
     """Per-rank compute on the current CUDA device through the C ABI (include/ozaki_b200.h)."""
 
@@ -36,6 +46,7 @@ class CudaOps:
         self.lib = self.engine.lib
         self.device = torch.device("cuda", torch.cuda.current_device())
         self._glob = {}
+        self._ws = {}
 
     @property
     def launches(self):
@@ -44,9 +55,6 @@ class CudaOps:
     def _stream(self):
         return torch.cuda.current_stream().cuda_stream
 
-    def buffers(self, rows, n, k, N):
-        return self.engine.buffers(rows, n, k, N)
-
     def colmax(self, A):
         rows, k = A.shape
         out = torch.empty(k, dtype=torch.int64, device=A.device)
@@ -54,51 +62,67 @@ class CudaOps:
         self.engine.launches += 1
         return out
 
-    def stats_finish(self, A, B, colmax, inside):
+    def rowmax(self, B):
+        k, cols = B.shape
+        out = torch.empty(k, dtype=torch.int64, device=B.device)
+        check(self.lib.ozk_stats_rowmax(ptr(B), k, cols, ptr(out), self._stream()), "ozk_stats_rowmax")
+        self.engine.launches += 1
+        return out
+
+    def local_stats(self, A, B, colmax, rowmax, inside):
+        """gamma from the global maxima, then this rank's row statistics of A and column statistics of B."""
         rows, k = A.shape
-        n = B.shape[1]
-        b = self.engine.buffers(rows, n, k, 20)
-        check(self.lib.ozk_stats_finish(ptr(A), ptr(B), rows, n, k, 1 if inside else 0, ptr(colmax), ptr(b["gam"]),
-                                        ptr(b["r"]), ptr(b["c"]), ptr(b["sA"]), ptr(b["nA"]), ptr(b["sB"]), ptr(b["nB"]),
-                                        ptr(b["flag"]), ptr(b["ws_stats"]), b["ws_stats"].numel(), self._stream()),
-              "ozk_stats_finish")
-        self.engine.launches += 5
+        cols = B.shape[1]
+        b = self.engine.buffers(rows, cols, k, 20)
+        st = self._stream()
+        check(self.lib.ozk_stats_gamma(ptr(colmax), ptr(rowmax), k, 1 if inside else 0, ptr(b["gam"]), ptr(b["flag"]),
+                                       st), "ozk_stats_gamma")
+        check(self.lib.ozk_stats_rows(ptr(A), rows, k, ptr(b["gam"]), ptr(b["r"]), ptr(b["sA"]), ptr(b["nA"]), st),
+              "ozk_stats_rows")
+        check(self.lib.ozk_stats_cols(ptr(B), k, cols, ptr(b["gam"]), ptr(b["c"]), ptr(b["sB"]), ptr(b["nB"]),
+                                      ptr(b["ws_stats"]), b["ws_stats"].numel(), st), "ozk_stats_cols")
+        self.engine.launches += 4
         return {"gam": b["gam"], "r": b["r"], "sA": b["sA"], "nA": b["nA"], "c": b["c"], "sB": b["sB"], "nB": b["nB"],
                 "flag": b["flag"], "_b": b}
 
-    def global_rows(self, m, device):
-        g = self._glob.get(m)
+    def global_stats(self, m, n, device):
+        g = self._glob.get((m, n))
         if g is None:
             g = {"r": torch.empty(m, dtype=torch.int32, device=device),
                  "sA": torch.empty(m, dtype=torch.float64, device=device),
-                 "nA": torch.empty(m, dtype=torch.float64, device=device)}
-            self._glob[m] = g
+                 "nA": torch.empty(m, dtype=torch.float64, device=device),
+                 "c": torch.empty(n, dtype=torch.int32, device=device),
+                 "sB": torch.empty(n, dtype=torch.float64, device=device),
+                 "nB": torch.empty(n, dtype=torch.float64, device=device)}
+            self._glob[(m, n)] = g
         return g
 
     def rule_prepare(self, st, glob, m, n, k, Ir, Jr, force_N, force_p):
         b = st["_b"]
-        ws = b.setdefault("ws_rule_global_" + str(m), torch.empty(max(1, self.lib.ozk_rule_workspace_bytes(m, n, k)),
-                                                                    dtype=torch.uint8, device=self.device))
-        check(self.lib.ozk_rule_prepare(ptr(glob["r"]), ptr(st["c"]), ptr(glob["sA"]), ptr(glob["nA"]), ptr(st["sB"]),
-                                        ptr(st["nB"]), ptr(st["flag"]), m, n, k, ptr(Ir), Ir.numel(), ptr(Jr), Jr.numel(),
-                                        int(force_N or 0), -1 if force_p is None else int(force_p), ptr(b["dec"]),
-                                        ptr(b["pdev"]), ptr(b["aux"]), ptr(ws), ws.numel(), self._stream()),
-              "ozk_rule_prepare")
+        key = (m, n, k)
+        ws = self._ws.get(key)
+        if ws is None:
+            ws = torch.empty(max(1, self.lib.ozk_rule_workspace_bytes(m, n, k)), dtype=torch.uint8, device=self.device)
+            self._ws = {key: ws}
+        check(self.lib.ozk_rule_prepare(ptr(glob["r"]), ptr(glob["c"]), ptr(glob["sA"]), ptr(glob["nA"]),
+                                        ptr(glob["sB"]), ptr(glob["nB"]), ptr(st["flag"]), m, n, k, ptr(Ir), Ir.numel(),
+                                        ptr(Jr), Jr.numel(), int(force_N or 0), -1 if force_p is None else int(force_p),
+                                        ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]), ptr(ws), ws.numel(),
+                                        self._stream()), "ozk_rule_prepare")
         self.engine.launches += 1
         return {"ws": ws, "b": b, "m": m, "n": n, "k": k}
 
-    def rule_probe(self, h, A, B, row_begin):
-        rows = A.shape[0]
+    def rule_probe(self, h, A, B, row_begin, col_begin):
         ws = h["ws"]
-        check(self.lib.ozk_rule_probe(ptr(A), ptr(B), row_begin, rows, h["m"], h["n"], h["k"], ptr(ws), ws.numel(),
-                                      self._stream()), "ozk_rule_probe")
+        check(self.lib.ozk_rule_probe_block(ptr(A), ptr(B), row_begin, A.shape[0], col_begin, B.shape[1], h["m"],
+                                            h["n"], h["k"], ptr(ws), ws.numel(), self._stream()), "ozk_rule_probe_block")
         self.engine.launches += 2
         off = self.lib.ozk_rule_probe_offset(h["m"], h["n"], h["k"])
         return ws[off:off + 96 * 96 * 8].view(torch.float64)
 
-    def rule_finish(self, h, st, glob, tau, safety):
+    def rule_finish(self, h, glob, tau, safety):
         b = h["b"]
-        check(self.lib.ozk_rule_finish(ptr(glob["r"]), ptr(st["c"]), ptr(glob["sA"]), ptr(st["sB"]), h["m"], h["n"],
+        check(self.lib.ozk_rule_finish(ptr(glob["r"]), ptr(glob["c"]), ptr(glob["sA"]), ptr(glob["sB"]), h["m"], h["n"],
                                        h["k"], float(tau), float(safety), ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]),
                                        ptr(h["ws"]), h["ws"].numel(), self._stream()), "ozk_rule_finish")
         self.engine.launches += 1
@@ -107,8 +131,8 @@ class CudaOps:
 
     def core(self, A, B, st, N, p, C):
         rows, k = A.shape
-        n = B.shape[1]
-        b = self.engine.buffers(rows, n, k, N)
+        cols = B.shape[1]
+        b = self.engine.buffers(rows, cols, k, N)
         if b is not st["_b"]:          # grown: copy the statistics into the new buffers
             for x in ("gam", "r", "c", "sA", "nA", "sB", "nB", "flag"):
                 b[x].copy_(st[x])
@@ -122,13 +146,18 @@ class CudaOps:
 
 
 class DistributedOzakiCRT:
-    """``run(A_local, B, C_local)``: this rank's rows of C = A B, with the plane count and scalings of the whole
-    product.  Every rank must call ``run`` with the same shapes and arguments (A_local: equal row counts)."""
+    """``run(A_block, B_block, C_block)``: this rank's block of C = A B, with the plane count and scalings of the
+    whole product.  Rank g = a S + b passes rows [a m/R, (a+1) m/R) of A and columns [b n/S, (b+1) n/S) of B (as a
+    contiguous k x n/S matrix); every rank must call ``run`` with the same block shapes and arguments.
+    ``grid=(R, S)`` (default ``default_grid(world)``)."""
 
-    def __init__(self, group=None, ops=None):
+    def __init__(self, group=None, ops=None, grid=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.R, self.S = grid if grid is not None else default_grid(self.world)
+        assert self.R * self.S == self.world, "grid must cover the ranks"
+        self.a, self.b = divmod(self.rank, self.S)
         self.ops = ops if ops is not None else CudaOps()
         self.probe = {}
 
@@ -150,39 +179,49 @@ class DistributedOzakiCRT:
                                torch.as_tensor(Jr, dtype=torch.int64, device=device))
         return self.probe[key]
 
+    def _gather(self, x, total, stride, count):
+        """all_gather of an equally sized per-rank vector; keeps the blocks of ranks 0, stride, 2 stride, ... (one per
+        row block when stride = S, one per column block when stride = 1 and count = S)."""
+        parts = torch.empty(self.world * x.numel(), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(parts, x.contiguous(), group=self.group)
+        parts = parts.view(self.world, x.numel())
+        return parts[0:stride * count:stride].reshape(total)
+
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, safety=2.0,
-            b_root=None, config=None):
+            config=None):
         if config is not None:
             force_N, force_p = int(config["N"]), config.get("p")
         rows, k = A.shape
-        n = B.shape[1]
-        assert B.shape[0] == k and rows % 4 == 0 and n % 32 == 0 and k % 32 == 0, "shape rule (per rank)"
-        m = rows * self.world
-        row_begin = rows * self.rank
+        cols = B.shape[1]
+        assert B.shape[0] == k and rows % 4 == 0 and cols % 32 == 0 and k % 32 == 0, "shape rule (per rank)"
+        m, n = rows * self.R, cols * self.S
+        row_begin, col_begin = rows * self.a, cols * self.b
         if C is None:
-            C = torch.empty((rows, n), dtype=torch.float64, device=A.device)
-        if b_root is not None:
-            dist.broadcast(B, src=b_root, group=self.group)
-        # 1. global column max of |A|
+            C = torch.empty((rows, cols), dtype=torch.float64, device=A.device)
+        # 1. global maxima -> gamma, flag; local statistics
         cm = self.ops.colmax(A)
-        dist.all_reduce(cm, op=dist.ReduceOp.MAX, group=self.group)
-        st = self.ops.stats_finish(A, B, cm, inside)
-        # 2. row statistics of all ranks
-        glob = self.ops.global_rows(m, A.device)
-        dist.all_gather_into_tensor(glob["r"], st["r"].contiguous(), group=self.group)
-        dist.all_gather_into_tensor(glob["sA"], st["sA"].contiguous(), group=self.group)
-        dist.all_gather_into_tensor(glob["nA"], st["nA"].contiguous(), group=self.group)
-        # 3. probe product summed over the row blocks, then the same decision everywhere
+        rm = self.ops.rowmax(B)
+        mx = torch.cat([cm, rm])
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=self.group)
+        st = self.ops.local_stats(A, B, mx[:k], mx[k:], inside)
+        # 2. statistics of all rows and columns
+        glob = self.ops.global_stats(m, n, A.device)
+        for x in ("r", "sA", "nA"):
+            glob[x].copy_(self._gather(st[x], m, self.S, self.R))
+        for x in ("c", "sB", "nB"):
+            glob[x].copy_(self._gather(st[x], n, 1, self.S))
+        # 3. probe product summed over the blocks, then the same decision everywhere
         Ir, Jr = self._probe_sets(m, n, seed, A.device)
         h = self.ops.rule_prepare(st, glob, m, n, k, Ir, Jr, force_N, force_p)
-        D = self.ops.rule_probe(h, A, B, row_begin)
+        D = self.ops.rule_probe(h, A, B, row_begin, col_begin)
         dist.all_reduce(D, op=dist.ReduceOp.SUM, group=self.group)
-        N, p, fb, preq, aux = self.ops.rule_finish(h, st, glob, tau, safety)
+        N, p, fb, preq, aux = self.ops.rule_finish(h, glob, tau, safety)
         if fb or N == 0:
             self.ops.native(A, B, C)
             return C, {"fallback": True, "preq": preq}
         self.ops.core(A, B, st, N, p, C)
-        return C, {"N": N, "p": p, "preq": preq, "rows": [row_begin, row_begin + rows], "world": self.world}
+        return C, {"N": N, "p": p, "preq": preq, "rows": [row_begin, row_begin + rows],
+                   "cols": [col_begin, col_begin + cols], "grid": [self.R, self.S], "world": self.world}
 
 
-__all__ = ["DistributedOzakiCRT", "CudaOps", "_lib"]
+__all__ = ["DistributedOzakiCRT", "CudaOps", "default_grid", "_lib"]

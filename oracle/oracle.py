@@ -52,7 +52,7 @@ def lib():
         P = ctypes.c_void_p
         i32, f64 = ctypes.c_int, ctypes.c_double
         L.ozo_stats.argtypes = [P, P, i32, i32, i32, i32, P, P, P, P, P, P, P, P]
-        L.ozo_stats_ext.argtypes = [P, P, i32, i32, i32, i32, P, P, P, P, P, P, P, P, P]
+        L.ozo_stats_ext.argtypes = [P, P, i32, i32, i32, i32, P, P, P, P, P, P, P, P, P, P]
         L.ozo_colmax.argtypes = [P, i32, i32, P]
         L.ozo_pmax_bits.argtypes = [i32, f64, f64, i32]
         L.ozo_pmax_bits.restype = i32
@@ -109,19 +109,33 @@ def colmax(A):
     return out.view(np.int64)
 
 
-def stats_given_colmax(A, B, colmax_global, inside=True):
-    """Statistics of a row block of A given the column max of |A| over all rows (row-sharded products)."""
+def rowmax(B):
+    """max over columns of the |B_lj| bit patterns (uint64 as int64)."""
+    B = _c64(B)
+    return (B.view(np.uint64) & np.uint64(0x7FFFFFFFFFFFFFFF)).max(axis=1).view(np.int64)
+
+
+def stats_given_maxima(A, B, colmax_global, rowmax_global=None, inside=True):
+    """Statistics of a row block of A and a column block of B given the column max of |A| over all rows and (if
+    given) the row max of |B| over all columns (blocked products)."""
     A, B = _c64(A), _c64(B)
     m, k = A.shape
     n = B.shape[1]
     cm = np.ascontiguousarray(np.asarray(colmax_global).view(np.uint64))
+    rm = None if rowmax_global is None else np.ascontiguousarray(np.asarray(rowmax_global).view(np.uint64))
     out = {"gam": np.zeros(k, np.int32), "r": np.zeros(m, np.int32), "c": np.zeros(n, np.int32),
            "sA": np.zeros(m), "nA": np.zeros(m), "sB": np.zeros(n), "nB": np.zeros(n)}
     flag = np.zeros(1, np.int32)
-    lib().ozo_stats_ext(_p(A), _p(B), m, n, k, 1 if inside else 0, _p(cm), _p(out["gam"]), _p(out["r"]), _p(out["c"]),
-                        _p(out["sA"]), _p(out["nA"]), _p(out["sB"]), _p(out["nB"]), _p(flag))
+    lib().ozo_stats_ext(_p(A), _p(B), m, n, k, 1 if inside else 0, _p(cm), None if rm is None else _p(rm),
+                        _p(out["gam"]), _p(out["r"]), _p(out["c"]), _p(out["sA"]), _p(out["nA"]), _p(out["sB"]),
+                        _p(out["nB"]), _p(flag))
     out["flag"] = int(flag[0])
     return out
+
+
+def stats_given_colmax(A, B, colmax_global, inside=True):
+    """Statistics of a row block of A given the column max of |A| over all rows (row-sharded products)."""
+    return stats_given_maxima(A, B, colmax_global, None, inside)
 
 
 def pmax_bits(N, nuA, nuB, k) -> int:

@@ -1,8 +1,9 @@
-"""The multi-GPU C row-block orchestration (matrix_numbers_b200.distributed) over gloo ranks on the CPU.
+"""The multi-GPU C block orchestration (matrix_numbers_b200.distributed) over gloo ranks on the CPU.
 
 The per-rank compute is supplied by ``OracleOps`` (the CPU oracle behind the ops interface of ``CudaOps``), so these
-tests check the collective steps and the index bookkeeping: the gathered C of 2 ranks must equal the single-process
-product bit for bit, and every rank must reach the same (N, p).  A failing rank must end the others' next collective
+tests check the collective steps and the index bookkeeping: the assembled C of 2 ranks (row blocks or column blocks)
+and of a 2 x 2 grid of 4 ranks must equal the single-process product bit for bit, and every rank must reach the same
+(N, p).  A failing rank must end the others' next collective
 with an error instead of a hang (host-side failure injection; no GPU involved)."""
 import os
 import socket
@@ -33,36 +34,41 @@ class OracleOps:
     def colmax(self, A):
         return torch.from_numpy(self.O.colmax(A.numpy()).copy())
 
-    def stats_finish(self, A, B, colmax, inside):
-        st = self.O.stats_given_colmax(A.numpy(), B.numpy(), colmax.numpy(), inside)
+    def rowmax(self, B):
+        return torch.from_numpy(self.O.rowmax(B.numpy()).copy())
+
+    def local_stats(self, A, B, colmax, rowmax, inside):
+        st = self.O.stats_given_maxima(A.numpy(), B.numpy(), colmax.numpy(), rowmax.numpy(), inside)
         out = {x: torch.from_numpy(np.ascontiguousarray(st[x])) for x in ("gam", "r", "sA", "nA", "c", "sB", "nB")}
         out["flag"] = torch.tensor([st["flag"]], dtype=torch.int32)
         out["_np"] = st
         return out
 
-    def global_rows(self, m, device):
+    def global_stats(self, m, n, device):
         return {"r": torch.empty(m, dtype=torch.int32), "sA": torch.empty(m, dtype=torch.float64),
-                "nA": torch.empty(m, dtype=torch.float64)}
+                "nA": torch.empty(m, dtype=torch.float64), "c": torch.empty(n, dtype=torch.int32),
+                "sB": torch.empty(n, dtype=torch.float64), "nB": torch.empty(n, dtype=torch.float64)}
 
     def rule_prepare(self, st, glob, m, n, k, Ir, Jr, force_N, force_p):
-        g = {"r": glob["r"].numpy(), "sA": glob["sA"].numpy(), "nA": glob["nA"].numpy(),
-             "c": st["c"].numpy(), "sB": st["sB"].numpy(), "nB": st["nB"].numpy(), "flag": int(st["flag"][0])}
+        g = {x: glob[x].numpy() for x in ("r", "sA", "nA", "c", "sB", "nB")}
+        g["flag"] = int(st["flag"][0])
         I = np.concatenate([Ir.numpy(), self.O.hard_top(g["r"], g["sA"], k)])
         J = np.concatenate([Jr.numpy(), self.O.hard_top(g["c"], g["sB"], k)])
         return {"g": g, "I": I, "J": J, "m": m, "n": n, "k": k, "force_N": force_N, "force_p": force_p}
 
-    def rule_probe(self, h, A, B, row_begin):
-        # this rank's probe rows of D = |A_I| |B_J|, zeros for the rows other ranks own (summed by all_reduce)
-        rows = A.shape[0]
+    def rule_probe(self, h, A, B, row_begin, col_begin):
+        # this rank's entries of D = |A_I| |B_J| (probe row and column inside its block), zeros elsewhere
+        rows, cols = A.shape[0], B.shape[1]
         D = np.zeros((96, 96))
         I, J = h["I"], h["J"]
+        jb = [b for b, j in enumerate(J) if col_begin <= j < col_begin + cols]
         for a, i in enumerate(I):
-            if row_begin <= i < row_begin + rows:
-                D[a, :len(J)] = self.O.probe_D(A.numpy(), B.numpy(), [i - row_begin], J)[0]
+            if row_begin <= i < row_begin + rows and jb:
+                D[a, jb] = self.O.probe_D(A.numpy(), B.numpy(), [i - row_begin], [J[b] - col_begin for b in jb])[0]
         h["Dt"] = torch.from_numpy(D.reshape(-1))
         return h["Dt"]
 
-    def rule_finish(self, h, st, glob, tau, safety):
+    def rule_finish(self, h, glob, tau, safety):
         I, J = h["I"], h["J"]
         D = h["Dt"].numpy().reshape(96, 96)[:len(I), :len(J)]
         ru = self.O.rule(h["g"], h["m"], h["n"], h["k"], I, J, D, tau, safety, h["force_N"])
@@ -82,6 +88,9 @@ class OracleOps:
         return C
 
 
+GRIDS = {"ok": (2, 1), "cols": (1, 2), "grid4": (2, 2)}
+
+
 def _worker(rank, world, port, outdir, mode):
     try:
         sys.path.insert(0, ROOT)
@@ -97,12 +106,14 @@ def _worker(rank, world, port, outdir, mode):
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
         from matrix_numbers_b200.distributed import DistributedOzakiCRT
-        m, k, n = 128, 256, 96
+        m, k, n = 128, 256, 128
         A, B = pkg.make_inputs(m, k, n, 2.0, seed=31)
-        rows = m // world
-        Al = torch.from_numpy(np.ascontiguousarray(A[rank * rows:(rank + 1) * rows]))
-        Bt = torch.from_numpy(B)
-        D = DistributedOzakiCRT(ops=OracleOps(O))
+        R, S = GRIDS[mode] if mode in GRIDS else (world, 1)
+        a, b = divmod(rank, S)
+        rows, cols = m // R, n // S
+        Al = torch.from_numpy(np.ascontiguousarray(A[a * rows:(a + 1) * rows]))
+        Bt = torch.from_numpy(np.ascontiguousarray(B[:, b * cols:(b + 1) * cols]))
+        D = DistributedOzakiCRT(ops=OracleOps(O), grid=(R, S))
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure on rank 1 before the first collective")
         C, info = D.run(Al, Bt)
@@ -130,21 +141,25 @@ def _spawn(world, mode, tmp_path):
     return alive
 
 
-def test_row_blocks_equal_single_process(oracle, tmp_path, pkg):
-    alive = _spawn(2, "ok", tmp_path)
+@pytest.mark.parametrize("mode,world", [("ok", 2), ("cols", 2), ("grid4", 4)])
+def test_blocks_equal_single_process(oracle, tmp_path, pkg, mode, world):
+    alive = _spawn(world, mode, tmp_path)
     assert not any(alive)
     errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]
     assert not errs, open(os.path.join(tmp_path, errs[0])).read()
-    A, B = pkg.make_inputs(128, 256, 96, 2.0, seed=31)
+    R, S = GRIDS[mode]
+    A, B = pkg.make_inputs(128, 256, 128, 2.0, seed=31)
+
+    def assemble(name):
+        return np.concatenate([np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{a * S + b}.npy"))
+                                               for b in range(S)], axis=1) for a in range(R)])
     Cref, iref = oracle.run(A, B)
-    C = np.concatenate([np.load(os.path.join(tmp_path, f"C_{r}.npy")) for r in range(2)])
-    np.testing.assert_array_equal(C.view(np.uint64), Cref.view(np.uint64))
-    infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(2)]
-    assert infos[0] == infos[1]
+    np.testing.assert_array_equal(assemble("C").view(np.uint64), Cref.view(np.uint64))
+    infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(world)]
+    assert all(i == infos[0] for i in infos)
     assert infos[0][:3] == (iref["N"], iref["p"], iref["p_req"])
     C22ref, i22 = oracle.run(A, B, force_N=22)
-    C22 = np.concatenate([np.load(os.path.join(tmp_path, f"C22_{r}.npy")) for r in range(2)])
-    np.testing.assert_array_equal(C22.view(np.uint64), C22ref.view(np.uint64))
+    np.testing.assert_array_equal(assemble("C22").view(np.uint64), C22ref.view(np.uint64))
     assert infos[0][3:] == (22, i22["p"])
 
 
