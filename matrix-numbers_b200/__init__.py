@@ -32,7 +32,7 @@ def __getattr__(name):
     if name in ("coprime_ip", "int8_crt", "chain_cost_model"):
         from . import planning
         return getattr(planning, name)
-    if name in ("make_inputs", "config_inputs", "Sample", "exact_sample", "CONFIGS"):
+    if name in ("make_inputs", "make_inputs_w", "config_inputs", "Sample", "exact_sample", "audit_bound", "CONFIGS"):
         from . import harness
         return getattr(harness, name)
     raise AttributeError(name)
@@ -40,5 +40,5 @@ def __getattr__(name):
 
 __all__ = ["OzakiCRT", "DistributedOzakiCRT", "PersistA", "full_certificate", "MODS", "NMAX", "NEG", "pmax_bits", "bound_matrix", "worst_case_p",
            "sigma_of", "make_config_table", "pick_config", "limbs_for", "_limbs_for", "_pow2tab", "modulus_product",
-           "make_inputs", "config_inputs", "Sample", "exact_sample", "CONFIGS", "coprime_ip", "int8_crt",
+           "make_inputs", "make_inputs_w", "config_inputs", "Sample", "exact_sample", "audit_bound", "CONFIGS", "coprime_ip", "int8_crt",
            "chain_cost_model", "_lib"]

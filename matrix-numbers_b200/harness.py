@@ -111,3 +111,32 @@ class Sample:
         with np.errstate(all="ignore"):
             e2 = np.where(self.absab > 0, d / self.absab, 0.0)
         return {"E1": float(d.max() / self.den1) if self.den1 > 0 else float(d.max()), "E2": float(e2.max())}
+
+
+def make_inputs_w(n, seed=0):
+    """The reference's rotated ill-scaled family W (make_inputs_ext, ozaki_engine.py:1618-1631), from numpy's generator:
+    A = rotate_rows(At diag(d)), B = rotate_cols(diag(d)^-1 Bt) with d_l = 2^(20 l / (n - 1)) and At, Bt standard
+    normal, so A B keeps 20 binades of column / row scaling that inside scaling has to undo."""
+    g = np.random.default_rng(1000 * seed + n + 7)
+    At = g.standard_normal((n, n))
+    Bt = g.standard_normal((n, n))
+    d = np.exp2(20.0 * np.arange(n) / (n - 1))
+    idx = (np.arange(n)[None, :] + np.arange(n)[:, None]) % n
+    A = np.take_along_axis(At * d[None, :], idx, axis=1)
+    B = np.take_along_axis(Bt / d[:, None], idx, axis=0)
+    return np.ascontiguousarray(A), np.ascontiguousarray(B)
+
+
+def audit_bound(S, info, k, C, scale=1.0):
+    """Lemma L1 audit on a Sample (the reference's audit_bound, ozaki_engine.py:1755-1766): |C_hat - C_ref| against
+    scale E_ij(p) + 2^-53 (|C_hat| + |C_ref|); returns violations and the worst ratio."""
+    from .constants import bound_matrix
+    h, p = info["stats"], info["p"]
+    Eb = scale * bound_matrix(h["r"], h["c"], h["sA"], h["sB"], k, p, S.ri, S.ci)
+    Cs = C[S.tri][:, S.tci].cpu().numpy()
+    err = np.abs(Cs - S.ref)
+    lim = Eb * (1 + 1e-9) + 2.0 ** -53 * (np.abs(Cs) + np.abs(S.ref)) * (1 + 1e-9)
+    nz = err > 0
+    return {"max_err_over_bound": float((err / lim).max()), "violations": int((err > lim).sum()),
+            "median_bound_over_err": float(np.median(Eb[nz] / err[nz])) if nz.any() else None,
+            "max_err_over_D": float((err / S.absab).max())}

@@ -1,0 +1,28 @@
+"""``run_host``: host buffers in and out, the core in row blocks with each finished block of C copied back while the
+next one computes.  Bit-exact against the device-resident ``run``; the fallback path fills the host C too."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("m,k,n,blocks", [(1000, 512, 256, 4), (256, 1024, 512, 1), (1536, 256, 128, 3)])
+def test_run_host_equals_run(pkg, engine, m, k, n, blocks):
+    import torch
+    A, B = pkg.make_inputs(m, k, n, 2.0, seed=m + n)
+    Ah, Bh = torch.from_numpy(A).pin_memory(), torch.from_numpy(B).pin_memory()
+    for _ in range(2):
+        Ch, info = engine.run_host(Ah, Bh, blocks=blocks)
+        assert not Ch.is_cuda and not info.get("fallback")
+        C, ir = engine.run(Ah.cuda(), Bh.cuda())
+        assert (info["N"], info["p"]) == (ir["N"], ir["p"])
+        assert np.array_equal(Ch.numpy(), C.cpu().numpy())
+
+
+def test_run_host_fallback(pkg, engine):
+    import torch
+    A, B = pkg.make_inputs(256, 256, 128, 1.0, seed=1)
+    B[7, 9] = np.inf
+    Ch, info = engine.run_host(torch.from_numpy(A), torch.from_numpy(B))
+    assert info.get("fallback")
+    assert np.array_equal(np.isinf(Ch.numpy()), np.isinf(A @ B))
