@@ -49,6 +49,8 @@ struct CertParams {
     const double* sA;
     const double* sB;
     double derate, tau, safety, f2k;   // 1 - 8 k 2^-24, tau, safety, 0.25 k
+    double inv_safety;                 // 1 / safety when safety is a power of two (then x / safety == x * inv_safety)
+    int safety_pow2;
     int m, n, k;
     unsigned long long* xmin;          // bit pattern of min xmax over certified entries (atomicMin)
     unsigned long long* uncertified;
@@ -57,17 +59,28 @@ struct CertParams {
 
 __device__ __forceinline__ double pow2i(int e) { return ldexp(1.0, e); }
 
+// g[l] = 2^gamma_l and ig[l] = 2^-gamma_l (torch.exp2 of the integer gamma, exact; ig is only used where it is a
+// finite power of two, so that x * ig[l] and x / g[l] are the same correctly rounded value)
+__global__ void cert_pow2_kernel(const int32_t* __restrict__ gam, int k, double* __restrict__ g, double* __restrict__ ig) {
+    const int l = blockIdx.x * blockDim.x + threadIdx.x;
+    if (l >= k) return;
+    g[l] = pow2i(gam[l]);
+    ig[l] = pow2i(-gam[l]);
+}
+
 // As = fp16(fp32((|A| (2^gamma 2^-r)) (1 - 2^-10))), 2 elements per thread; row scales 2^r_i as a by-product
-__global__ void cert_prep_a_kernel(const double* __restrict__ A, const int32_t* __restrict__ gam,
+__global__ void cert_prep_a_kernel(const double* __restrict__ A, const double* __restrict__ g,
                                    const int32_t* __restrict__ r, int m, int k, __half2* __restrict__ A16,
                                    double* __restrict__ rowscale) {
+    const double2* g2 = reinterpret_cast<const double2*>(g);
     for (int i = blockIdx.y; i < m; i += gridDim.y) {
         const double sr = pow2i(-r[i]);
         if (blockIdx.x == 0 && threadIdx.x == 0) rowscale[i] = pow2i(r[i]);
         const double2* row = reinterpret_cast<const double2*>(A + (size_t)i * k);
         for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < k / 2; h += gridDim.x * blockDim.x) {
             const double2 v = __ldg(row + h);
-            const double f0 = __dmul_rn(pow2i(gam[2 * h]), sr), f1 = __dmul_rn(pow2i(gam[2 * h + 1]), sr);
+            const double2 gg = __ldg(g2 + h);
+            const double f0 = __dmul_rn(gg.x, sr), f1 = __dmul_rn(gg.y, sr);
             const double x0 = __dmul_rn(__dmul_rn(fabs(v.x), f0), 1.0 - 0x1p-10);
             const double x1 = __dmul_rn(__dmul_rn(fabs(v.y), f1), 1.0 - 0x1p-10);
             A16[(size_t)i * (k / 2) + h] = __halves2half2(__float2half_rn(__double2float_rn(x0)),
@@ -76,11 +89,13 @@ __global__ void cert_prep_a_kernel(const double* __restrict__ A, const int32_t* 
     }
 }
 
-// Bs^T[j][l] = fp16(fp32((|B_lj| (2^-c_j / 2^gamma_l)) (1 - 2^-10))), through a 64 x 64 shared tile
+// Bs^T[j][l] = fp16(fp32((|B_lj| (2^-c_j / 2^gamma_l)) (1 - 2^-10))), through a 64 x 64 shared tile; the division
+// by the power of two 2^gamma_l is a multiplication by 2^-gamma_l (the same rounded value) where that is finite
 constexpr int kT = 64;
-__global__ void __launch_bounds__(256) cert_prep_b_kernel(const double* __restrict__ B, const int32_t* __restrict__ gam,
-                                                          const int32_t* __restrict__ c, int k, int n,
-                                                          __half* __restrict__ B16t, double* __restrict__ colscale) {
+__global__ void __launch_bounds__(256) cert_prep_b_kernel(const double* __restrict__ B, const double* __restrict__ g,
+                                                          const double* __restrict__ ig, const int32_t* __restrict__ c,
+                                                          int k, int n, __half* __restrict__ B16t,
+                                                          double* __restrict__ colscale) {
     __shared__ __half tile[kT][kT + 2];
     const int l0 = blockIdx.y * kT, j0 = blockIdx.x * kT;
     const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4
@@ -91,7 +106,8 @@ __global__ void __launch_bounds__(256) cert_prep_b_kernel(const double* __restri
         const int l = l0 + yy;
         __half h = __float2half_rn(0.0f);
         if (l < k && j < n) {
-            const double f = __ddiv_rn(scj, pow2i(gam[l]));
+            const double igl = __ldg(ig + l);
+            const double f = igl < INFINITY ? __dmul_rn(scj, igl) : __ddiv_rn(scj, __ldg(g + l));
             const double x = __dmul_rn(__dmul_rn(fabs(__ldg(B + (size_t)l * n + j)), f), 1.0 - 0x1p-10);
             h = __float2half_rn(__double2float_rn(x));
         }
@@ -119,14 +135,21 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int32_t* e
     atomicOr(err, code);
 }
 
-// the bound of one entry, in the reference's operation order; returns xmax, sets `ok` to D > 0
-__device__ __forceinline__ double entry_xmax(float dl, double rI, double cJ, double sAi, double sBj, const CertParams& p,
-                                             bool& ok, double& D) {
-    D = __dmul_rn(__dmul_rn(__dmul_rn((double)dl, p.derate), rI), cJ);
-    ok = D > 0.0;
-    const double thr = __ddiv_rn(__dmul_rn(p.tau, D), p.safety);
-    const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, sBj), __dmul_rn(cJ, sAi)));
-    const double F2 = __dmul_rn(__dmul_rn(p.f2k, rI), cJ);
+// fast approximations (hardware reciprocal / reciprocal square root), used only to skip entries
+__device__ __forceinline__ double rcp_approx(double x) {
+    double r;
+    asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(x));
+    return r;
+}
+__device__ __forceinline__ double rsqrt_approx(double x) {
+    double r;
+    asm("rsqrt.approx.f64 %0, %1;" : "=d"(r) : "d"(x));
+    return r;
+}
+
+// xmax of one entry, in the reference's operation order: thr = (tau D) / safety, F1 = 0.5 (rI sB + cJ sA),
+// F2 = ((0.25 k) rI) cJ, xmax = (2 thr) / (F1 + sqrt(F1 F1 + (4 F2) thr))
+__device__ __forceinline__ double entry_xmax(double thr, double F1, double F2) {
     const double disc = __dadd_rn(__dmul_rn(F1, F1), __dmul_rn(__dmul_rn(4.0, F2), thr));
     return __ddiv_rn(__dmul_rn(2.0, thr), __dadd_rn(F1, __dsqrt_rn(disc)));
 }
@@ -267,6 +290,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const bool rv = row < m;
             const double rI = rv ? cp.rowscale[row] : 0.0, sAi = rv ? cp.sA[row] : 0.0;
+            const double f2r = __dmul_rn(cp.f2k, rI);                // (0.25 k) 2^r_i
+            // the smallest xmax found so far by any CTA: entries whose lower bound is above it are skipped
+            {
+                const unsigned long long gb = *reinterpret_cast<volatile unsigned long long*>(cp.xmin);
+                best = gb < best ? gb : best;
+            }
 #pragma unroll 1
             for (int cc = 0; cc < 4; cc++) {
                 const int col_local = half * 128 + cc * 32;
@@ -275,19 +304,29 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_wait_ld();
                 const int col0 = tn * BN + col_local;
                 if (rv && col0 < n) {            // n % 32 == 0: the 32 columns are all in range or all out
+                    // every xmax >= min(thr / (2 F1), sqrt(thr / F2) / 2) (sqrt(F1^2 + 4 F2 thr) <= F1 + 2 sqrt(F2 thr));
+                    // that bound, from approximate reciprocals, lowered by 2^-8 (far above their error), decides
+                    // whether an entry can still be the minimum; only then is the reference formula evaluated
+                    const double bestd = best == kEmpty ? INFINITY : __longlong_as_double((long long)best);
 #pragma unroll
                     for (int e = 0; e < 32; e++) {   // fully unrolled: v[] stays in registers
                         const int col = col0 + e;
-                        bool ok;
-                        double D;
-                        const double x = entry_xmax(__uint_as_float(v[e]), rI, cp.colscale[col], sAi, cp.sB[col], cp, ok, D);
-                        if (ok) {
-                            const unsigned long long xb = (unsigned long long)__double_as_longlong(x);
-                            if (!(x != x) && xb < best) best = xb;   // NaN bounds are not minima
-                        } else {
-                            unc++;
-                        }
+                        const double cJ = cp.colscale[col];
+                        const double D = __dmul_rn(__dmul_rn(__dmul_rn((double)__uint_as_float(v[e]), cp.derate), rI), cJ);
                         if (cp.dbg_D) cp.dbg_D[(size_t)row * n + col] = D;
+                        if (!(D > 0.0)) { unc++; continue; }
+                        const double tD = __dmul_rn(cp.tau, D);
+                        const double thr = cp.safety_pow2 ? __dmul_rn(tD, cp.inv_safety) : __ddiv_rn(tD, cp.safety);
+                        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cp.sB[col]), __dmul_rn(cJ, sAi)));
+                        const double F2 = __dmul_rn(f2r, cJ);
+                        const double r1 = thr * rcp_approx(2.0 * F1);
+                        const double t = thr * rcp_approx(F2);
+                        const double r2 = 0.5 * t * rsqrt_approx(t);
+                        const double L = (r1 < r2 ? r1 : r2) * (1.0 - 0x1p-8);
+                        if (L >= bestd && L < INFINITY) continue;       // cannot be below the current minimum
+                        const double x = entry_xmax(thr, F1, F2);
+                        const unsigned long long xb = (unsigned long long)__double_as_longlong(x);
+                        if (!(x != x) && xb < best) best = xb;           // NaN bounds are not minima
                     }
                 }
             }
@@ -295,16 +334,15 @@ __global__ void __launch_bounds__(THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(acce_bar(b));
             acc_it++;
+            // publish the warp's minimum after every tile, so that the other CTAs can skip against it
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+                best = ob < best ? ob : best;
+            }
+            if (lane == 0 && best != kEmpty) atomicMin(cp.xmin, best);
         }
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long ob = __shfl_down_sync(0xffffffffu, best, o);
-            best = ob < best ? ob : best;
-            unc += __shfl_down_sync(0xffffffffu, unc, o);
-        }
-        if (lane == 0) {
-            if (best != kEmpty) atomicMin(cp.xmin, best);
-            if (unc) atomicAdd(cp.uncertified, unc);
-        }
+        for (int o = 16; o > 0; o >>= 1) unc += __shfl_down_sync(0xffffffffu, unc, o);
+        if (lane == 0 && unc) atomicAdd(cp.uncertified, unc);
     }
 
     tc_fence_before();
@@ -358,7 +396,7 @@ bool g_attr[64];
 extern "C" size_t ozk_certificate_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
     return align256((size_t)m * k * 2) + align256((size_t)n * k * 2) + align256((size_t)m * 8) + align256((size_t)n * 8) +
-           256;
+           2 * align256((size_t)k * 8) + 256;
 }
 
 extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, int k, const int32_t* gam,
@@ -390,13 +428,17 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     __half* B16t = reinterpret_cast<__half*>(ws + align256((size_t)m * k * 2));
     double* rowscale = reinterpret_cast<double*>(ws + align256((size_t)m * k * 2) + align256((size_t)n * k * 2));
     double* colscale = rowscale + align256((size_t)m * 8) / 8;
+    double* g = colscale + align256((size_t)n * 8) / 8;
+    double* ig = g + align256((size_t)k * 8) / 8;
 
     if (cudaMemsetAsync(xmin, 0xFF, 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
     if (cudaMemsetAsync(uncertified, 0, 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
     const int bx = (k / 2 + 255) / 256 < 8 ? (k / 2 + 255) / 256 : 8;
-    cert_prep_a_kernel<<<dim3(bx, m < 65535 ? m : 65535), 256, 0, st>>>(A, gam, r, m, k, reinterpret_cast<__half2*>(A16), rowscale);
+    cert_pow2_kernel<<<(k + 255) / 256, 256, 0, st>>>(gam, k, g, ig);
     OZK_CHECK_LAUNCH();
-    cert_prep_b_kernel<<<dim3((n + kT - 1) / kT, (k + kT - 1) / kT), 256, 0, st>>>(B, gam, c, k, n, B16t, colscale);
+    cert_prep_a_kernel<<<dim3(bx, m < 65535 ? m : 65535), 256, 0, st>>>(A, g, r, m, k, reinterpret_cast<__half2*>(A16), rowscale);
+    OZK_CHECK_LAUNCH();
+    cert_prep_b_kernel<<<dim3((n + kT - 1) / kT, (k + kT - 1) / kT), 256, 0, st>>>(B, g, ig, c, k, n, B16t, colscale);
     OZK_CHECK_LAUNCH();
 
     CUtensorMap ta, tb;
@@ -411,6 +453,12 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     cp.derate = 1.0 - 8.0 * (double)k * 0x1p-24;
     cp.tau = tau;
     cp.safety = safety;
+    {
+        int e2 = 0;
+        const double fr = frexp(safety, &e2);
+        cp.safety_pow2 = (fr == 0.5) ? 1 : 0;                  // safety = 2^(e2 - 1)
+        cp.inv_safety = cp.safety_pow2 ? ldexp(1.0, 1 - e2) : 0.0;
+    }
     cp.f2k = 0.25 * (double)k;
     cp.m = m;
     cp.n = n;

@@ -306,11 +306,12 @@ def test_gemm_residues_k_segments(pkg, oracle, torch_mod, k):
 
 
 # ------------------------------------------------------------------------------------------------ reconstruction
-@pytest.mark.parametrize("N", [1, 6, 8, 14, 16, 19, 20, 21, 30, 32])
-def test_reconstruct_random_residues(pkg, oracle, torch_mod, N):
-    """Uniform random residues: every CRT value in [0, M) occurs, including |X| close to M/2."""
+@pytest.mark.parametrize("N,n", [(N, 256) for N in range(1, 33)] + [(N, 36) for N in (6, 16, 19, 32)])
+def test_reconstruct_random_residues(pkg, oracle, torch_mod, N, n):
+    """Uniform random residues: every CRT value in [0, M) occurs, including |X| close to M/2; every plane count, and
+    rows that are not a multiple of the 4-element vectors' 32-byte sectors (n = 36)."""
     torch = torch_mod
-    m, n = 64, 256
+    m = 64
     rng = np.random.default_rng(N)
     X = np.stack([rng.integers(0, pkg.MODS[t], size=(m, n)) for t in range(N)]).astype(np.uint8)
     r = rng.integers(-40, 40, size=m).astype(np.int32)
