@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-accuracy", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=0, help="rows = cols of the CPU sample block (0: auto)")
-    ap.add_argument("--mode", default="sampled", choices=["sampled", "certified", "config", "persist"],
+    ap.add_argument("--mode", default="sampled", choices=["sampled", "certified", "config", "persist", "chain"],
                     help="sampled: the reference's timed path (default); certified: the plane count from the "
                          "full-matrix certificate; config: the single-graph path with (N, p) given (the sampled "
                          "rule's choice); persist: PersistA, A encoded once per step and --q products")
@@ -207,11 +207,55 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------ residue chain
+def bench_chain(args):
+    """--mode chain (single GPU): an exact integer chain A_1 A_2 A_3 of the workload's square size n with 8-bit
+    entries, kept in INT8 residue form between the products (matrix_numbers_b200.chain); the plane count is the
+    reference model's fixed base for R = H^3 n^2, H = 255.  Metric: exact integer TOPS = 2 n^3 (q - 1) / t."""
+    import torch
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(0)
+    _, _, n, _, _, _, desc = pkg.CONFIGS[args.workload]
+    q, b = 3, 8
+    rs = np.random.RandomState(0)
+    mats = [torch.from_numpy(rs.randint(-255, 256, size=(n, n)).astype(np.float64)).cuda() for _ in range(q)]
+    ch = pkg.ResidueChain()
+    for _ in range(args.warmup):
+        _, info = ch.product(mats, b=b)
+    torch.cuda.synchronize()
+    l0 = ch.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0, None) as clocks:
+        time.sleep(0.3)
+        e0.record()
+        for _ in range(args.steps):
+            _, info = ch.product(mats, b=b)
+        e1.record()
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / args.steps
+    ops = 2.0 * n ** 3 * (q - 1)
+    peak = int8_peak_tops(torch, torch.device("cuda", 0))
+    int8_ops = ops * info["N"]
+    print(json.dumps({"metric": f"exact integer chain TOPS (A1 A2 A3, {b}-bit entries, residue form)",
+                      "value": ops / t / 1e12, "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
+                      "vs_baseline": None, "dtype": "int8 residues", "data": "synthetic",
+                      "config": {"workload": args.workload, "n": n, "q": q, "bits": b, "planes": info["N"],
+                                 "gemms_per_step": info["gemms"], "mode": "chain"},
+                      "roofline": {"bound": "tensor", "achieved": int8_ops / t / 1e12, "peak": peak,
+                                   "unit": "TOPS (INT8, whole chain incl. splits and reconstruction)",
+                                   "frac": int8_ops / t / 1e12 / peak, "traffic": None},
+                      "clocks": clocks.summary(), "gpu_launches": ch.launches - l0}), flush=True)
+
+
 # ------------------------------------------------------------------------------------------------ our arm
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.mode == "chain":
+        bench_chain(args)
         return
     import torch
     import torch.distributed as dist

@@ -177,6 +177,13 @@ int ozk_gemm_i32(const int8_t* A_plane, const int8_t* B_plane, int m, int n, int
 int ozk_reconstruct(const uint8_t* X, const int32_t* r, const int32_t* c, const int32_t* p_dev, int m, int n, int N,
                     double* C, ozk_stream_t stream);
 
+/* ---- residue chains (the chain cost law of code/digit_gemm.py:1252-1291, executed): the product planes of
+ * ozk_gemm_residues, X[t] in [0, m_t), mapped to the symmetric int8 residues of the split,
+ * out[t][e] = X[t][e] - m_t when X[t][e] >= ceil(m_t / 2), else X[t][e]; so that a product stays in residue form
+ * and is the left operand of the next product.  plane_elems = elements per plane (a multiple of 16); X and out
+ * 16-byte aligned; out may be X itself.                                                                      */
+int ozk_residue_symmetric(const uint8_t* X, int N, size_t plane_elems, int8_t* out, ozk_stream_t stream);
+
 /* ---- stage 3 in one call (replaces OzakiCRT.core, ozaki_engine.py:1310-1350): split A (unless skip_a),
  * split B, products, reconstruction.                                                                        */
 int ozk_core(const double* A, const double* B, const int32_t* gam, const int32_t* r, const int32_t* c,

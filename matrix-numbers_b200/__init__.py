@@ -29,6 +29,9 @@ def __getattr__(name):
     if name in ("full_certificate",):
         from . import certificate
         return getattr(certificate, name)
+    if name in ("ResidueChain", "planes_for", "chain_bound"):
+        from . import chain
+        return getattr(chain, name)
     if name in ("coprime_ip", "int8_crt", "chain_cost_model"):
         from . import planning
         return getattr(planning, name)
@@ -41,4 +44,4 @@ def __getattr__(name):
 __all__ = ["OzakiCRT", "DistributedOzakiCRT", "PersistA", "full_certificate", "MODS", "NMAX", "NEG", "pmax_bits", "bound_matrix", "worst_case_p",
            "sigma_of", "make_config_table", "pick_config", "limbs_for", "_limbs_for", "_pow2tab", "modulus_product",
            "make_inputs", "make_inputs_w", "config_inputs", "Sample", "exact_sample", "audit_bound", "CONFIGS", "coprime_ip", "int8_crt",
-           "chain_cost_model", "_lib"]
+           "chain_cost_model", "ResidueChain", "planes_for", "chain_bound", "_lib"]

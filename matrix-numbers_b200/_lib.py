@@ -49,6 +49,7 @@ _SIGNATURES = {
     "ozk_rule_probe_block": ([P, P, I32, I32, I32, I32, I32, I32, I32, P, SZ, P], I32),
     "ozk_rule_finish": ([P, P, P, P, I32, I32, I32, F64, F64, P, P, P, P, SZ, P], I32),
     "ozk_rule": ([P, P, I32, I32, I32, P, P, P, P, P, P, P, P, I32, P, I32, F64, F64, I32, I32, P, P, P, P, SZ, P], I32),
+    "ozk_residue_symmetric": ([P, I32, SZ, P, P], I32),
     "ozk_split_a": ([P, P, P, P, I32, I32, I32, P, P], I32),
     "ozk_split_b": ([P, P, P, P, I32, I32, I32, P, P], I32),
     "ozk_gemm_residues": ([P, P, I32, I32, I32, I32, P, P, P], I32),

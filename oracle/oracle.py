@@ -341,6 +341,38 @@ def full_certificate(A, B, st, tau=2.0 ** -52, safety=2.0):
             "xmax": xmax}
 
 
+def chain_exact(mats):
+    """Exact product A_1 A_2 ... A_q of integer matrices as Python integers (numpy object arrays), the value an exact
+    residue chain must reproduce (code/digit_gemm.py:1252-1291 models its cost: one INT8 GEMM per modulus per
+    product, residues reduced after every product).  Returns the object array."""
+    out = np.asarray(mats[0]).astype(np.int64).astype(object)
+    for A in mats[1:]:
+        out = out.dot(np.asarray(A).astype(np.int64).astype(object))
+    return out
+
+
+def chain_residues(mats, N):
+    """The chain computed the way the residue form computes it: per modulus m_t (the first N of MODS) the running
+    product is reduced modulo m_t after every product and mapped to the split's symmetric range
+    [-floor(m/2), ceil(m/2) - 1] (ozaki_engine.py:989-995) before the next one; the last product is left in
+    [0, m_t) (the GEMM epilogue's range, ozaki_engine.py:952-967).  int64 arithmetic (|products| < 2^63 for the
+    dimensions tests use).  Returns uint8 planes (N, m, n)."""
+    planes = []
+    for t in range(N):
+        P = MODS[t]
+
+        def sym(x):
+            x = np.mod(x, P)
+            return np.where(x >= (P + 1) // 2, x - P, x)
+        cur = sym(np.asarray(mats[0]).astype(np.int64))
+        for s, A in enumerate(mats[1:]):
+            cur = np.mod(cur @ sym(np.asarray(A).astype(np.int64)), P)
+            if s + 2 < len(mats):
+                cur = sym(cur)
+        planes.append(cur.astype(np.uint8))
+    return np.stack(planes)
+
+
 def _split(a):
     t = 134217729.0 * a
     hi = t - (t - a)
