@@ -126,15 +126,27 @@ __device__ __forceinline__ void mma_k32(int (&d)[4], const unsigned* a, unsigned
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(cA), "r"(cA), "r"(cB), "r"(cB));
 }
 
-// Per-lane constants of one 16-modulus row tile (moduli t0 + g and t0 + g + 8 of lane (g, tig)).  The lane-dependent
-// indices into constant memory are read once per thread.
+// d += A B (m16n8k32, u8 x u8 -> s32), the accumulator carried in d
+__device__ __forceinline__ void mma_k32_acc(int (&d)[4], const unsigned* a, unsigned b0, unsigned b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Per-lane constants of one row tile: the moduli of rows g and g + 8 of lane (g, tig) -- t0 + g and t0 + g + 8 for a
+// 16-modulus tile, or the pair chosen by the packed tail below.  The lane-dependent indices into constant memory are
+// read once per thread.
 template <int KB>
 struct TileConsts {
     unsigned a[KB / 8];   // A fragment: {row g, row g+8} of bytes 4 tig .. 4 tig + 3 (k32: and 16 + 4 tig ..)
     unsigned MA, MB, nPA, nPB;
     __device__ __forceinline__ void init(int t0) {
-        const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-        const int tA = t0 + g, tB = t0 + g + 8;   // < 32 = OZK_NMAX
+        const int g = (threadIdx.x & 31) >> 2;
+        init_rows(t0 + g, t0 + g + 8);
+    }
+    __device__ __forceinline__ void init_rows(int tA, int tB) {   // tA, tB < 32 = OZK_NMAX
+        const int tig = threadIdx.x & 3;
         if (KB == 16) {
             a[0] = c_split.W16[tA][tig];
             a[1] = c_split.W16[tB][tig];
@@ -215,6 +227,61 @@ __device__ __forceinline__ void chunk_residues(const unsigned (&b)[KB / 4], cons
     if (needB && tB < N) *reinterpret_cast<uint2*>(o + (size_t)tB * plane_bytes) = make_uint2(wB[0], wB[1]);
 }
 
+// Moduli 16 .. N-1 for 16 < N <= 20 (16-byte strings): a 16-row tile of one chunk would leave most rows idle, so
+// the rows are (chunk, modulus) pairs instead -- G chunks x E = 16 / G moduli (G = 8 for N <= 18, 4 for N <= 20).
+// Row g (and g + 8) of lane (g, tig) is chunk c = g % G of the group with modulus 16 + g / G (and 16 + g / G + 8 / G);
+// its weights are non-zero only on the k-half of m16n8k32 product q that holds chunk c's string (chunks 2q and
+// 2q + 1 fill k 0-15 and 16-31), so the G / 2 products of a chain sum exactly each row's own chunk.  One chain per
+// n-tile, accumulated onto 0; h is added on the integer pipe.  `pc` holds the lane's two moduli (init_rows).
+template <int G>
+__device__ __forceinline__ void packed_tail(const unsigned char* wsm, int chunk_bytes, const TileConsts<16>& pc,
+                                            int N, int cnt, int8_t* o0, size_t chunk_stride, size_t plane_bytes) {
+    const int g = (threadIdx.x & 31) >> 2;
+    const int c = g % G, tA = 16 + g / G, tB = tA + 8 / G;
+    const int hA = (int)((0u - pc.nPA) >> 1), hB = (int)((0u - pc.nPB) >> 1);
+    const int tig = threadIdx.x & 3;
+#pragma unroll
+    for (int grp = 0; grp < 8 / G; grp++) {
+        unsigned wA[2], wB[2];
+#pragma unroll
+        for (int half = 0; half < 2; half++) {          // n-tiles 2 half and 2 half + 1: few live accumulators
+            int d[2][4];
+#pragma unroll
+            for (int q = 0; q < G / 2; q++) {
+                const bool mine = (c >> 1) == q, odd = (c & 1) != 0;
+                const unsigned a[4] = {mine && !odd ? pc.a[0] : 0u, mine && !odd ? pc.a[1] : 0u,
+                                       mine && odd ? pc.a[0] : 0u, mine && odd ? pc.a[1] : 0u};
+                const unsigned char* c0 = wsm + (grp * G + 2 * q) * chunk_bytes;
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const int j = 2 * half + u;          // the n-tile's word tig of element row 8j + (g ^ 2j)
+                    const int roff = (8 * j + (g ^ (2 * j))) * kRowBytes + 4 * tig;
+                    const unsigned b0 = *reinterpret_cast<const unsigned*>(c0 + roff);
+                    const unsigned b1 = *reinterpret_cast<const unsigned*>(c0 + chunk_bytes + roff);
+                    if (q == 0) mma_k32(d[u], a, b0, b1, 0, 0);
+                    else mma_k32_acc(d[u], a, b0, b1);
+                }
+            }
+            int rA[4], rB[4];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                rA[2 * u] = residue(d[u][0] + hA, d[u][0], pc.MA, pc.nPA);
+                rA[2 * u + 1] = residue(d[u][1] + hA, d[u][1], pc.MA, pc.nPA);
+                rB[2 * u] = residue(d[u][2] + hB, d[u][2], pc.MB, pc.nPB);
+                rB[2 * u + 1] = residue(d[u][3] + hB, d[u][3], pc.MB, pc.nPB);
+            }
+            wA[half] = pack_s8(rA[0], rA[1], rA[2], rA[3]);
+            wB[half] = pack_s8(rB[0], rB[1], rB[2], rB[3]);
+        }
+        const int ch = grp * G + c;
+        if (ch < cnt) {
+            int8_t* o = o0 + (size_t)ch * chunk_stride;
+            if (tA < N) *reinterpret_cast<uint2*>(o + (size_t)tA * plane_bytes) = make_uint2(wA[0], wA[1]);
+            if (tB < N) *reinterpret_cast<uint2*>(o + (size_t)tB * plane_bytes) = make_uint2(wB[0], wB[1]);
+        }
+    }
+}
+
 // One kernel for both operands.  A "vector" v is a row of A (v = i) or a column of B (v = j); its elements are
 // indexed by the contraction index l and its planes are out[t][v][l] (K-major).  A chunk is 32 consecutive l of one
 // vector (k % 32 == 0).  A warp task is TC chunks (TC = 8 for KB = 16, 4 for KB = 32), loaded with TC independent
@@ -224,7 +291,7 @@ __device__ __forceinline__ void chunk_residues(const unsigned (&b)[KB / 4], cons
 //   B: TC adjacent columns of one l-block; lane (rg, c) = (lane / TC, lane % TC) loads rows TC rg + i (i < TC) of
 //      column c, so that each load instruction reads whole sectors.  Tasks run along l first, so the warps of a
 //      block write adjacent pieces of the same plane rows.
-template <int KB, bool IS_B>
+template <int KB, bool IS_B, bool PACKED>
 __device__ __forceinline__ void split_tasks(const double* __restrict__ src, const int32_t* __restrict__ vexp,
                                             const int32_t* __restrict__ gam, int p, int V, int k, int N,
                                             int8_t* __restrict__ out, unsigned char* wsm) {
@@ -239,9 +306,17 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
     const int ntasks = IS_B ? (V / TC) * lblocks : (nchunks + TC - 1) / TC;
     const int gwarp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
+    // moduli 16 .. N-1: a second 16-modulus tile per chunk, or for 16 < N <= 20 the packed tail (16-byte strings;
+    // a separate instantiation, launched only for those N, so that the common path keeps its register budget)
+    constexpr bool packed = PACKED && KB == 16;
     TileConsts<KB> tc0, tc1;
     tc0.init(0);
-    tc1.init(16);
+    if constexpr (packed) {
+        const int g = lane >> 2, G = N <= 18 ? 8 : 4;
+        tc1.init_rows(16 + g / G, 16 + g / G + 8 / G);
+    } else {
+        tc1.init(16);
+    }
     // task coordinates, advanced by the grid stride without divisions in the loop:
     //   A: (v, lb) of the task's first chunk;  B: (vector group, l-block)
     const int step = IS_B ? nwarps : nwarps * TC;
@@ -302,8 +377,14 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
                 unsigned b[KB / 4];
                 chunk_fragments<KB>(wsm + i * kChunkBytes, b);
                 chunk_residues<KB>(b, tc0, 0, N, o, plane_bytes);
-                if (N > 16) chunk_residues<KB>(b, tc1, 16, N, o, plane_bytes);
+                if (N > 16 && !packed) chunk_residues<KB>(b, tc1, 16, N, o, plane_bytes);
             }
+        }
+        if constexpr (packed) {
+            int8_t* o0 = IS_B ? out + (size_t)(cv * TC) * k + 32 * clb + 8 * tig : out + (size_t)task * TC * 32 + 8 * tig;
+            const size_t stride = IS_B ? (size_t)k : (size_t)32;
+            if (N <= 18) packed_tail<8>(wsm, kChunkBytes, tc1, N, cnt, o0, stride, plane_bytes);
+            else packed_tail<4>(wsm, kChunkBytes, tc1, N, cnt, o0, stride, plane_bytes);
         }
         cv += sv;
         clb += slb;
@@ -311,7 +392,7 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
     }
 }
 
-template <bool IS_B>
+template <bool IS_B, bool PACKED>
 __global__ void __launch_bounds__(kWarps * 32, OZK_SPLIT_MINB) split_kernel(const double* __restrict__ src,
                                                                const int32_t* __restrict__ vexp,
                                                                const int32_t* __restrict__ gam,
@@ -320,8 +401,8 @@ __global__ void __launch_bounds__(kWarps * 32, OZK_SPLIT_MINB) split_kernel(cons
     __shared__ __align__(16) unsigned char strings[kWarps][kWarpSmem];
     const int p = *p_dev;
     unsigned char* wsm = strings[threadIdx.x >> 5];
-    if (p <= 119) split_tasks<16, IS_B>(src, vexp, gam, p, V, k, N, out, wsm);
-    else split_tasks<32, IS_B>(src, vexp, gam, p, V, k, N, out, wsm);
+    if (p <= 119) split_tasks<16, IS_B, PACKED>(src, vexp, gam, p, V, k, N, out, wsm);
+    else split_tasks<32, IS_B, false>(src, vexp, gam, p, V, k, N, out, wsm);
 }
 
 int split_blocks(long long tasks) {
@@ -342,7 +423,10 @@ extern "C" int ozk_split_a(const double* A, const int32_t* r, const int32_t* gam
     if ((long long)m * (k >> 5) >= 0x7fffffffLL - (1LL << 24)) return OZK_ERR_ARG;   // chunk indices in 31 bits
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
     const long long tasks = ((long long)m * (k >> 5) + 7) / 8;
-    split_kernel<false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares);
+    if (N > 16 && N <= 20)
+        split_kernel<false, true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares);
+    else
+        split_kernel<false, false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }
@@ -355,7 +439,10 @@ extern "C" int ozk_split_b(const double* B, const int32_t* c, const int32_t* gam
     if ((long long)n * (k >> 5) >= 0x7fffffffLL - (1LL << 24)) return OZK_ERR_ARG;   // chunk indices in 31 bits
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
     const long long tasks = (long long)(n / 8) * (k >> 5);
-    split_kernel<true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres);
+    if (N > 16 && N <= 20)
+        split_kernel<true, true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres);
+    else
+        split_kernel<true, false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }

@@ -239,6 +239,23 @@ def test_split_ragged(pkg, oracle, torch_mod, m, k, n, N, p):
     assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, N))
 
 
+# moduli 16 .. N-1 for 16 < N <= 20 come from the packed tail (8 chunks x 2 moduli or 4 chunks x 4 moduli per MMA
+# row tile): every N around it, a last A task with fewer than 8 chunks, one and several l-blocks per B column group
+@pytest.mark.parametrize("m,k,n,N", [(52, 96, 64, 17), (20, 32, 96, 18), (36, 160, 32, 19), (12, 224, 64, 20),
+                                     (28, 96, 32, 21), (1028, 128, 160, 18), (44, 64, 288, 20)])
+def test_split_packed_tail(pkg, oracle, torch_mod, m, k, n, N):
+    torch = torch_mod
+    A, B = pkg.make_inputs(m, k, n, 2.0, seed=3 * m + N)
+    A[0, 1], B[2, 0] = -5e-324, -0.0
+    Ad, Bd = T(torch, A), T(torch, B)
+    st = dev_stats(pkg, torch, Ad, Bd)
+    sto = oracle.stats(A, B, True)
+    for p in (58, 67, 119):
+        Ar, Br = dev_split(pkg, torch, Ad, Bd, st, p, N)
+        assert np.array_equal(Ar, oracle.split_A(A, sto["r"], sto["gam"], p, N)), p
+        assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, N)), p
+
+
 # ------------------------------------------------------------------------------------------------ INT8 products
 def rand_planes(rng, N, rows, k):
     return rng.integers(-128, 128, size=(N, rows, k), dtype=np.int64).astype(np.int8)
