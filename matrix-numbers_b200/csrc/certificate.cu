@@ -48,7 +48,9 @@ struct CertParams {
     const double* colscale;   // 2^c_j
     const double* sA;
     const double* sB;
+    const double* colg;                // sB_j / 2^c_j (the skip test's column term)
     double derate, tau, safety, f2k;   // 1 - 8 k 2^-24, tau, safety, 0.25 k
+    double kappa;                      // safety / (tau derate)
     double inv_safety;                 // 1 / safety when safety is a power of two (then x / safety == x * inv_safety)
     int safety_pow2;
     int m, n, k;
@@ -95,13 +97,17 @@ constexpr int kT = 64;
 __global__ void __launch_bounds__(256) cert_prep_b_kernel(const double* __restrict__ B, const double* __restrict__ g,
                                                           const double* __restrict__ ig, const int32_t* __restrict__ c,
                                                           int k, int n, __half* __restrict__ B16t,
-                                                          double* __restrict__ colscale) {
+                                                          double* __restrict__ colscale, const double* __restrict__ sB,
+                                                          double* __restrict__ colg) {
     __shared__ __half tile[kT][kT + 2];
     const int l0 = blockIdx.y * kT, j0 = blockIdx.x * kT;
     const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4
     const int j = j0 + tx;
-    if (blockIdx.y == 0 && ty == 0 && j < n) colscale[j] = pow2i(c[j]);
     const double scj = j < n ? pow2i(-c[j]) : 0.0;
+    if (blockIdx.y == 0 && ty == 0 && j < n) {
+        colscale[j] = pow2i(c[j]);
+        colg[j] = sB[j] * scj;          // sB_j / 2^c_j (inf or NaN when 2^-c_j overflows: then nothing is skipped)
+    }
     for (int yy = ty; yy < kT; yy += 4) {
         const int l = l0 + yy;
         __half h = __float2half_rn(0.0f);
@@ -135,7 +141,7 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int32_t* e
     atomicOr(err, code);
 }
 
-// fast approximations (hardware reciprocal / reciprocal square root), used only to skip entries
+// fast approximations (hardware reciprocal / reciprocal square root, errors far below 2^-8), used only to skip entries
 __device__ __forceinline__ double rcp_approx(double x) {
     double r;
     asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(x));
@@ -291,6 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool rv = row < m;
             const double rI = rv ? cp.rowscale[row] : 0.0, sAi = rv ? cp.sA[row] : 0.0;
             const double f2r = __dmul_rn(cp.f2k, rI);                // (0.25 k) 2^r_i
+            const double hI = rv ? __ddiv_rn(sAi, rI) : 0.0;           // sA_i / 2^r_i (the skip test's row term)
             // the smallest xmax found so far by any CTA: entries whose lower bound is above it are skipped
             {
                 const unsigned long long gb = *reinterpret_cast<volatile unsigned long long*>(cp.xmin);
@@ -304,26 +311,38 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_wait_ld();
                 const int col0 = tn * BN + col_local;
                 if (rv && col0 < n) {            // n % 32 == 0: the 32 columns are all in range or all out
-                    // every xmax >= min(thr / (2 F1), sqrt(thr / F2) / 2) (sqrt(F1^2 + 4 F2 thr) <= F1 + 2 sqrt(F2 thr));
-                    // that bound, from approximate reciprocals, lowered by 2^-8 (far above their error), decides
-                    // whether an entry can still be the minimum; only then is the reference formula evaluated
+                    // every xmax >= min(thr / (2 F1), sqrt(thr / F2) / 2) (sqrt(F1^2 + 4 F2 thr) <= F1 + 2 sqrt(F2 thr)).
+                    // With D = v derate 2^r_i 2^c_j, that bound is >= b = best (1 + 2^-8) exactly when
+                    //   v >= beta (g_j + h_i),  beta = b safety / (tau derate), g_j = sB_j / 2^c_j, h_i = sA_i / 2^r_i,
+                    //   v >= T2 = b^2 k safety / (tau derate);
+                    // the 2^-8 margin is far above the rounding of these and of the reference formula, so such an
+                    // entry cannot be below the current minimum and is skipped.  No skipping while the thresholds
+                    // could underflow (b < 2^-400, g_j + h_i < 2^-1000) or when they overflow or are NaN.  That bound
+                    // can be 2x below xmax; an entry it keeps is then tested with the formula itself, evaluated with
+                    // the approximate reciprocal and reciprocal square root and lowered by 2^-8, and only an entry
+                    // within that margin of the minimum (or one whose estimate is not finite) is evaluated exactly.
                     const double bestd = best == kEmpty ? INFINITY : __longlong_as_double((long long)best);
+                    const double bm = bestd * (1.0 + 0x1p-8);
+                    const bool can_skip = bm >= 0x1p-400 && cp.kappa > 0.0 && cp.kappa < INFINITY;
+                    const double beta = can_skip ? bm * cp.kappa : INFINITY;
+                    const double T2 = can_skip ? bm * bm * (double)cp.k * cp.kappa : INFINITY;
 #pragma unroll
                     for (int e = 0; e < 32; e++) {   // fully unrolled: v[] stays in registers
                         const int col = col0 + e;
                         const double cJ = cp.colscale[col];
-                        const double D = __dmul_rn(__dmul_rn(__dmul_rn((double)__uint_as_float(v[e]), cp.derate), rI), cJ);
+                        const double vd = (double)__uint_as_float(v[e]);
+                        const double D = __dmul_rn(__dmul_rn(__dmul_rn(vd, cp.derate), rI), cJ);
                         if (cp.dbg_D) cp.dbg_D[(size_t)row * n + col] = D;
                         if (!(D > 0.0)) { unc++; continue; }
+                        const double gh = cp.colg[col] + hI;
+                        if (vd >= T2 && vd >= beta * gh && gh >= 0x1p-1000) continue;
                         const double tD = __dmul_rn(cp.tau, D);
                         const double thr = cp.safety_pow2 ? __dmul_rn(tD, cp.inv_safety) : __ddiv_rn(tD, cp.safety);
                         const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cp.sB[col]), __dmul_rn(cJ, sAi)));
                         const double F2 = __dmul_rn(f2r, cJ);
-                        const double r1 = thr * rcp_approx(2.0 * F1);
-                        const double t = thr * rcp_approx(F2);
-                        const double r2 = 0.5 * t * rsqrt_approx(t);
-                        const double L = (r1 < r2 ? r1 : r2) * (1.0 - 0x1p-8);
-                        if (L >= bestd && L < INFINITY) continue;       // cannot be below the current minimum
+                        const double disc = fma(F1, F1, 4.0 * F2 * thr);
+                        const double L = 2.0 * thr * rcp_approx(F1 + disc * rsqrt_approx(disc)) * (1.0 - 0x1p-8);
+                        if (L >= bestd && L < INFINITY) continue;
                         const double x = entry_xmax(thr, F1, F2);
                         const unsigned long long xb = (unsigned long long)__double_as_longlong(x);
                         if (!(x != x) && xb < best) best = xb;           // NaN bounds are not minima
@@ -395,8 +414,8 @@ bool g_attr[64];
 
 extern "C" size_t ozk_certificate_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
-    return align256((size_t)m * k * 2) + align256((size_t)n * k * 2) + align256((size_t)m * 8) + align256((size_t)n * 8) +
-           2 * align256((size_t)k * 8) + 256;
+    return align256((size_t)m * k * 2) + align256((size_t)n * k * 2) + align256((size_t)m * 8) +
+           2 * align256((size_t)n * 8) + 2 * align256((size_t)k * 8) + 256;
 }
 
 extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, int k, const int32_t* gam,
@@ -430,6 +449,7 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     double* colscale = rowscale + align256((size_t)m * 8) / 8;
     double* g = colscale + align256((size_t)n * 8) / 8;
     double* ig = g + align256((size_t)k * 8) / 8;
+    double* colg = ig + align256((size_t)k * 8) / 8;
 
     if (cudaMemsetAsync(xmin, 0xFF, 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
     if (cudaMemsetAsync(uncertified, 0, 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
@@ -438,7 +458,8 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     OZK_CHECK_LAUNCH();
     cert_prep_a_kernel<<<dim3(bx, m < 65535 ? m : 65535), 256, 0, st>>>(A, g, r, m, k, reinterpret_cast<__half2*>(A16), rowscale);
     OZK_CHECK_LAUNCH();
-    cert_prep_b_kernel<<<dim3((n + kT - 1) / kT, (k + kT - 1) / kT), 256, 0, st>>>(B, g, ig, c, k, n, B16t, colscale);
+    cert_prep_b_kernel<<<dim3((n + kT - 1) / kT, (k + kT - 1) / kT), 256, 0, st>>>(B, g, ig, c, k, n, B16t, colscale, sB,
+                                                                                       colg);
     OZK_CHECK_LAUNCH();
 
     CUtensorMap ta, tb;
@@ -450,6 +471,7 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     cp.colscale = colscale;
     cp.sA = sA;
     cp.sB = sB;
+    cp.colg = colg;
     cp.derate = 1.0 - 8.0 * (double)k * 0x1p-24;
     cp.tau = tau;
     cp.safety = safety;
@@ -460,6 +482,7 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
         cp.inv_safety = cp.safety_pow2 ? ldexp(1.0, 1 - e2) : 0.0;
     }
     cp.f2k = 0.25 * (double)k;
+    cp.kappa = safety / (tau * cp.derate);
     cp.m = m;
     cp.n = n;
     cp.k = k;
