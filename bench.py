@@ -35,6 +35,9 @@ sys.path.insert(0, ROOT)
 import __graft_entry__  # noqa: E402
 
 METRIC = "emulated FP64 GEMM TFLOPS (2MNK/t) at n=16384, 1-8 B200; max rel error"
+# DRAM bytes (read + write) of one gemm_tc_kernel launch on one GPU, from one-pass ncu captures of this bench's own
+# command (profiles/dram_traffic_c3_n16384.md); workloads without a capture report null
+GEMM_TRAFFIC_BYTES = {"c3": 66.9e9 + 4.8e9, "c2": 537.7e6 + 242.9e6}
 
 
 def parse():
@@ -368,7 +371,9 @@ def main():
                 "peak": peak_int8, "unit": "TOPS (INT8)", "frac": achieved / peak_int8,
                 "peak_source": "cuBLASLt INT8 GEMM 8192^3 burst measured in this run (torch._int_mm)",
                 "bf16_measured_tflops_x2": 2 * bf16_peak, "frac_of_2x_bf16": achieved / (2 * bf16_peak),
-                "traffic": None, "algorithmic_ops_per_launch": int8_ops, "ms_per_launch": t_gemm * 1e3,
+                "traffic": GEMM_TRAFFIC_BYTES.get(args.workload) if world == 1 and args.mode == "sampled" else None,
+                "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                "algorithmic_ops_per_launch": int8_ops, "ms_per_launch": t_gemm * 1e3,
                 "stages_ms": {k_: v * 1e3 / 3 for k_, v in prof.items()}, "timed_call_stages_ms": in_step}
 
     # accuracy on a sample (rank 0's block): E1 / E2 against the correctly rounded product, native DGEMM beside it
