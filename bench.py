@@ -375,6 +375,14 @@ def main():
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                 "algorithmic_ops_per_launch": int8_ops, "ms_per_launch": t_gemm * 1e3,
                 "stages_ms": {k_: v * 1e3 / 3 for k_, v in prof.items()}, "timed_call_stages_ms": in_step}
+    # the emulated-FP64 ceiling is the INT8 rate over the plane count (one INT8 product per plane); the residue split
+    # moves (8 + N)(rows k + k cols) bytes (FP64 in, N planes out) against the measured copy bandwidth
+    t_split = prof["residues"] / 3
+    split_bytes = (8.0 + Nplanes) * (rows * k + k * cols)
+    roofline["emulated_ceiling_tflops"] = peak_int8 / Nplanes
+    roofline["frac_of_int8_over_N"] = (2.0 * rows * cols * k / (t_dev / products) / 1e12) / (peak_int8 / Nplanes)
+    roofline["split"] = {"bound": "hbm", "achieved": split_bytes / t_split / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": split_bytes / t_split / 1e9 / hbm_peak, "bytes_per_call": split_bytes}
 
     # accuracy on a sample (rank 0's block): E1 / E2 against the correctly rounded product, native DGEMM beside it
     acc = None
