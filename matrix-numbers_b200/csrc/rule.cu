@@ -23,7 +23,8 @@ namespace {
 
 constexpr int kProbeMax = 96;          // at most 64 random + 32 hard indices per side
 constexpr int kPrepThreads = 1024;
-constexpr int kFinalThreads = 1024;
+constexpr int kFinalThreads = 256;
+constexpr int kFinalBlocks = (kProbeMax * kProbeMax + kFinalThreads - 1) / kFinalThreads;   // one probe entry per thread
 constexpr int kProbeThreads = 256;
 constexpr int kProbeK = 16;            // contraction rows per smem tile of the probe product
 constexpr double kOnePlus = 1.0 + 1e-9;
@@ -38,6 +39,9 @@ struct RuleCtl {            // lives at the start of the workspace
     double nuA, nuB;
     int I[kProbeMax];
     int J[kProbeMax];
+    int preq_max;                    // the rule's final kernels: largest per-entry p so far
+    unsigned int fin_count;          // blocks of the last kernel that are done
+    unsigned long long worst_bits;   // largest E / D at p_req (bit pattern of a non-negative double)
 };
 
 __device__ __forceinline__ bool fits(int p, double nuA, double nuB, double sk, double M) {
@@ -198,7 +202,14 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
         return;
     }
     const int hr = min(32, m), hc = min(32, n);
-    if (threadIdx.x == 0) { ctl->done = 0; ctl->nI = nIr + hr; ctl->nJ = nJr + hc; }
+    if (threadIdx.x == 0) {
+        ctl->done = 0;
+        ctl->nI = nIr + hr;
+        ctl->nJ = nJr + hc;
+        ctl->preq_max = 1;
+        ctl->fin_count = 0u;
+        ctl->worst_bits = 0ull;
+    }
     // caller-supplied probe indices are clamped into range (an out-of-range index must not be dereferenced)
     for (int x = threadIdx.x; x < nIr; x += blockDim.x) ctl->I[x] = (Ir[x] >= 0 && Ir[x] < m) ? (int)Ir[x] : 0;
     for (int x = threadIdx.x; x < nJr; x += blockDim.x) ctl->J[x] = (Jr[x] >= 0 && Jr[x] < n) ? (int)Jr[x] : 0;
@@ -289,97 +300,119 @@ __device__ __forceinline__ bool ok_entry(const EntryTerms& t, int p, double safe
     return __dmul_rn(E, safety) <= t.rhs;
 }
 
-__global__ void __launch_bounds__(kFinalThreads) rule_final_kernel(
+// The rule's last step over the probe entries, one entry per thread on kFinalBlocks blocks.
+// rule_preq_kernel: the smallest p of every entry with D > 0 (closed-form start, then the exact comparisons of the
+// host rule), the maximum over the entries into ctl->preq_max.
+__global__ void __launch_bounds__(kFinalThreads) rule_preq_kernel(
     const int32_t* __restrict__ r, const int32_t* __restrict__ c, const double* __restrict__ sA,
     const double* __restrict__ sB, int k, double tau, double safety, const double* __restrict__ Dg,
-    RuleCtl* __restrict__ ctl, int32_t* __restrict__ dec, int32_t* __restrict__ p_dev, double* __restrict__ aux) {
+    RuleCtl* __restrict__ ctl) {
     if (ctl->done) return;
-    __shared__ int s_red[32];
-    __shared__ double s_redd[32];
-    __shared__ int s_preq;
+    __shared__ int s_red[kFinalThreads / 32];
     const int nI = ctl->nI, nJ = ctl->nJ;
-    const int cnt = nI * nJ;
-    const double k4 = 0.25 * (double)k;
-    // pass 1: smallest p per entry, maximum over entries
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
     int mx = 1;
-    for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
+    if (e < nI * nJ) {
         const int a = e / nJ, b = e % nJ;
         const double D = Dg[a * kProbeMax + b];
-        if (!(D > 0.0)) continue;
-        const int i = ctl->I[a], j = ctl->J[b];
-        EntryTerms t;
-        const int ri = r[i], cj = c[j];
-        t.F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(ldexp(1.0, ri), sB[j]), __dmul_rn(ldexp(1.0, cj), sA[i])));
-        t.F2 = __dmul_rn(k4, ldexp(1.0, ri + cj));
-        t.rhs = __dmul_rn(tau, D);
-        // closed-form start (largest 2^-p meeting E <= tau D / safety), then exact fix-up
-        const double cq = tau * D / safety;
-        const double xm = 2.0 * cq / (t.F1 + sqrt(t.F1 * t.F1 + 4.0 * t.F2 * cq));
-        const double est = ceil(-log2(xm));
-        int p = est != est ? 250 : (est < 1.0 ? 1 : (est > 250.0 ? 250 : (int)est));
-        while (p > 1 && ok_entry(t, p - 1, safety)) p--;
-        while (p < 250 && !ok_entry(t, p, safety)) p++;
-        mx = max(mx, p);
+        if (D > 0.0) {
+            const int i = ctl->I[a], j = ctl->J[b];
+            const int ri = r[i], cj = c[j];
+            EntryTerms t;
+            t.F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(ldexp(1.0, ri), sB[j]), __dmul_rn(ldexp(1.0, cj), sA[i])));
+            t.F2 = __dmul_rn(0.25 * (double)k, ldexp(1.0, ri + cj));
+            t.rhs = __dmul_rn(tau, D);
+            // closed-form start (largest 2^-p meeting E <= tau D / safety), then exact fix-up
+            const double cq = tau * D / safety;
+            const double xm = 2.0 * cq / (t.F1 + sqrt(t.F1 * t.F1 + 4.0 * t.F2 * cq));
+            const double est = ceil(-log2(xm));
+            int p = est != est ? 250 : (est < 1.0 ? 1 : (est > 250.0 ? 250 : (int)est));
+            while (p > 1 && ok_entry(t, p - 1, safety)) p--;
+            while (p < 250 && !ok_entry(t, p, safety)) p++;
+            mx = p;
+        }
     }
     for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_down_sync(0xffffffffu, mx, o));
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
     __syncthreads();
     if (threadIdx.x == 0) {
         int v = 1;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) v = max(v, s_red[w]);
-        s_preq = v;
+        for (int w = 0; w < kFinalThreads / 32; w++) v = max(v, s_red[w]);
+        atomicMax(&ctl->preq_max, v);
     }
-    __syncthreads();
-    const int preq = min(s_preq, 249);
-    // pass 2: worst E / D at p_req (the host rule's info, :1297-1298)
+}
+
+// rule_final_kernel: the worst E / D at p_req (the host rule's info, :1297-1298), maximum over the entries into
+// ctl->worst_bits; the last block to finish (a counter, no waiting) makes the decision: N = the smallest plane count
+// in [6, 32] whose pmax_bits reaches p_req, fallback when none does or p_req > 249; it also counts the distinct probe
+// rows and columns (the reference reports len(set(I)), len(set(J))) and resets the control fields for another call.
+__global__ void __launch_bounds__(kFinalThreads) rule_final_kernel(
+    const int32_t* __restrict__ r, const int32_t* __restrict__ c, const double* __restrict__ sA,
+    const double* __restrict__ sB, int k, double tau, double safety, const double* __restrict__ Dg,
+    RuleCtl* __restrict__ ctl, int32_t* __restrict__ dec, int32_t* __restrict__ p_dev, double* __restrict__ aux) {
+    if (ctl->done) return;
+    __shared__ double s_redd[kFinalThreads / 32];
+    __shared__ int s_last, s_du, s_dv;
+    const int nI = ctl->nI, nJ = ctl->nJ;
+    const int preq_all = ctl->preq_max;          // written by rule_preq_kernel, earlier on the stream
+    const int preq = min(preq_all, 249);
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
     double worst = 0.0;
-    for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
+    if (e < nI * nJ) {
         const int a = e / nJ, b = e % nJ;
         const double D = Dg[a * kProbeMax + b];
-        if (!(D > 0.0)) continue;
-        const int i = ctl->I[a], j = ctl->J[b];
-        const int ri = r[i], cj = c[j];
-        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(ldexp(1.0, ri), sB[j]), __dmul_rn(ldexp(1.0, cj), sA[i])));
-        const double F2 = __dmul_rn(k4, ldexp(1.0, ri + cj));
-        const double E = __dadd_rn(__dmul_rn(F1, ldexp(1.0, -preq)), __dmul_rn(F2, ldexp(1.0, -2 * preq)));
-        worst = fmax(worst, __ddiv_rn(E, D));
+        if (D > 0.0) {
+            const int i = ctl->I[a], j = ctl->J[b];
+            const int ri = r[i], cj = c[j];
+            const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(ldexp(1.0, ri), sB[j]), __dmul_rn(ldexp(1.0, cj), sA[i])));
+            const double F2 = __dmul_rn(0.25 * (double)k, ldexp(1.0, ri + cj));
+            const double E = __dadd_rn(__dmul_rn(F1, ldexp(1.0, -preq)), __dmul_rn(F2, ldexp(1.0, -2 * preq)));
+            worst = fmax(worst, __ddiv_rn(E, D));
+        }
     }
     for (int o = 16; o > 0; o >>= 1) worst = fmax(worst, __shfl_down_sync(0xffffffffu, worst, o));
     if ((threadIdx.x & 31) == 0) s_redd[threadIdx.x >> 5] = worst;
     __syncthreads();
     if (threadIdx.x == 0) {
         double w = 0.0;
-        for (int q = 0; q < (int)(blockDim.x >> 5); q++) w = fmax(w, s_redd[q]);
-        int N = 0, p = 0;
-        const bool over = s_preq > 249;
-        if (!over) {
-            for (int q = 6; q <= OZK_NMAX; q++)
-                if (ctl->pv[q] >= preq) { N = q; p = ctl->pv[q]; break; }
-        }
-        const int fb = N == 0;
-        dec[0] = N; dec[1] = p; dec[2] = fb; dec[3] = preq;
-        *p_dev = p;
-        aux[0] = ctl->nuA; aux[1] = ctl->nuB; aux[2] = w;
-        aux[5] = 0.0; aux[6] = 0.0; aux[7] = 0.0;
+        for (int q = 0; q < kFinalThreads / 32; q++) w = fmax(w, s_redd[q]);
+        atomicMax(&ctl->worst_bits, (unsigned long long)__double_as_longlong(w));   // w >= 0: bits order as values
+        __threadfence();
+        s_last = atomicAdd(&ctl->fin_count, 1u) == gridDim.x - 1 ? 1 : 0;
+        s_du = 0;
+        s_dv = 0;
     }
-    // distinct probe rows and columns (the reference reports len(set(I)), len(set(J))): an index counts when no
-    // earlier entry holds it; one thread per entry
-    __shared__ int s_du, s_dv;
-    if (threadIdx.x == 0) { s_du = 0; s_dv = 0; }
     __syncthreads();
+    if (!s_last) return;
+    __threadfence();
     if (threadIdx.x < nI) {
         const int a = threadIdx.x, v = ctl->I[a];
         bool seen = false;
         for (int b = 0; b < a; b++) seen |= ctl->I[b] == v;
         if (!seen) atomicAdd(&s_du, 1);
-    } else if (threadIdx.x >= 512 && threadIdx.x - 512 < nJ) {
-        const int a = threadIdx.x - 512, v = ctl->J[a];
+    } else if (threadIdx.x >= 128 && threadIdx.x - 128 < nJ) {
+        const int a = threadIdx.x - 128, v = ctl->J[a];
         bool seen = false;
         for (int b = 0; b < a; b++) seen |= ctl->J[b] == v;
         if (!seen) atomicAdd(&s_dv, 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) { aux[3] = (double)s_du; aux[4] = (double)s_dv; }
+    if (threadIdx.x == 0) {
+        const double w = __longlong_as_double((long long)atomicAdd(&ctl->worst_bits, 0ull));
+        int N = 0, p = 0;
+        if (preq_all <= 249) {
+            for (int q = 6; q <= OZK_NMAX; q++)
+                if (ctl->pv[q] >= preq) { N = q; p = ctl->pv[q]; break; }
+        }
+        dec[0] = N; dec[1] = p; dec[2] = N == 0; dec[3] = preq;
+        *p_dev = p;
+        aux[0] = ctl->nuA; aux[1] = ctl->nuB; aux[2] = w;
+        aux[3] = (double)s_du; aux[4] = (double)s_dv;
+        aux[5] = 0.0; aux[6] = 0.0; aux[7] = 0.0;
+        ctl->preq_max = 1;
+        ctl->worst_bits = 0ull;
+        ctl->fin_count = 0u;
+    }
 }
 
 int probe_blocks(int k) {
@@ -496,7 +529,9 @@ extern "C" int ozk_rule_finish(const int32_t* r, const int32_t* c, const double*
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
     RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
     const double* D = reinterpret_cast<const double*>(static_cast<char*>(workspace) + ozk_rule_probe_offset(m, n, k));
-    rule_final_kernel<<<1, kFinalThreads, 0, st>>>(r, c, sA, sB, k, tau, safety, D, ctl, dec, p_dev, aux);
+    rule_preq_kernel<<<kFinalBlocks, kFinalThreads, 0, st>>>(r, c, sA, sB, k, tau, safety, D, ctl);
+    OZK_CHECK_LAUNCH();
+    rule_final_kernel<<<kFinalBlocks, kFinalThreads, 0, st>>>(r, c, sA, sB, k, tau, safety, D, ctl, dec, p_dev, aux);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }

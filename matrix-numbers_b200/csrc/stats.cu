@@ -180,24 +180,51 @@ __global__ void __launch_bounds__(kThreads) colstats_b_kernel(const double* __re
     pq[o] = r0.q; pq[o + 1] = r1.q;
 }
 
-// chunk partials combined in chunk order: c_j = max of the local maxima (0 when the column has no non-zero, as the
-// consumers of c do at :1257, :1060), sB_j = sum, nB_j = sum of the partials rescaled to c_j
-__global__ void colstats_final_kernel(const int32_t* __restrict__ pc, const double* __restrict__ ps,
-                                      const double* __restrict__ pq, int nchunks, int n, int32_t* __restrict__ c,
-                                      double* __restrict__ sB, double* __restrict__ nB) {
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= n) return;
+// chunk partials combined: c_j = max of the local maxima (0 when the column has no non-zero, as the consumers of c do
+// at :1257, :1060), sB_j = sum, nB_j = sum of the partials rescaled to c_j.  One block per 32 columns (lane = column,
+// so every chunk row is read coalesced) and kFinWarps warps over the chunks (warp w: chunks w, w + kFinWarps, ...);
+// the warps' results are combined in warp order, so the sums have a fixed order (bitwise reproducible).
+constexpr int kFinWarps = 8;
+__global__ void __launch_bounds__(kFinWarps * 32) colstats_final_kernel(const int32_t* __restrict__ pc,
+                                                                        const double* __restrict__ ps,
+                                                                        const double* __restrict__ pq, int nchunks,
+                                                                        int n, int32_t* __restrict__ c,
+                                                                        double* __restrict__ sB,
+                                                                        double* __restrict__ nB) {
+    __shared__ int smx[kFinWarps][32];
+    __shared__ double sms[kFinWarps][32], smq[kFinWarps][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int j = blockIdx.x * 32 + lane;
+    const bool ok = j < n;
     int mx = OZK_NEG;
-    for (int h = 0; h < nchunks; h++) mx = max(mx, pc[(size_t)h * n + j]);
+    if (ok)
+        for (int h = w; h < nchunks; h += kFinWarps) mx = max(mx, __ldg(pc + (size_t)h * n + j));
+    smx[w][lane] = mx;
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kFinWarps; u++) mx = max(mx, smx[u][lane]);
     double s = 0.0, q = 0.0;
-    for (int h = 0; h < nchunks; h++) {
-        const int e = pc[(size_t)h * n + j];
-        s += ps[(size_t)h * n + j];
-        if (e != OZK_NEG) q += scale2(pq[(size_t)h * n + j], -2 * (mx - e));
+    if (ok)
+        for (int h = w; h < nchunks; h += kFinWarps) {
+            const size_t o = (size_t)h * n + j;
+            const int e = __ldg(pc + o);
+            s += __ldg(ps + o);
+            if (e != OZK_NEG) q += scale2(__ldg(pq + o), -2 * (mx - e));
+        }
+    sms[w][lane] = s;
+    smq[w][lane] = q;
+    __syncthreads();
+    if (w == 0 && ok) {
+        double S = 0.0, Q = 0.0;
+#pragma unroll
+        for (int u = 0; u < kFinWarps; u++) {
+            S += sms[u][lane];
+            Q += smq[u][lane];
+        }
+        sB[j] = S;
+        nB[j] = Q;
+        c[j] = mx <= OZK_NEG / 2 ? 0 : mx;
     }
-    sB[j] = s;
-    nB[j] = q;
-    c[j] = mx <= OZK_NEG / 2 ? 0 : mx;
 }
 
 }  // namespace
@@ -248,7 +275,7 @@ extern "C" int ozk_stats_finish(const double* A, const double* B, int m, int n, 
     const dim3 g2((n / 2 + kThreads - 1) / kThreads, nchunks);
     colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, chunk, pc, ps, pq);
     OZK_CHECK_LAUNCH();
-    colstats_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
+    colstats_final_kernel<<<(n + 31) / 32, kFinWarps * 32, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }
@@ -308,7 +335,7 @@ extern "C" int ozk_stats_cols(const double* B, int k, int n, const int32_t* gam,
     const dim3 g2((n / 2 + kThreads - 1) / kThreads, nchunks);
     colstats_b_kernel<<<g2, kThreads, 0, st>>>(B, gam, k, n, chunk, pc, ps, pq);
     OZK_CHECK_LAUNCH();
-    colstats_final_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
+    colstats_final_kernel<<<(n + 31) / 32, kFinWarps * 32, 0, st>>>(pc, ps, pq, nchunks, n, c, sB, nB);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }

@@ -125,7 +125,7 @@ class CudaOps:
         check(self.lib.ozk_rule_finish(ptr(glob["r"]), ptr(glob["c"]), ptr(glob["sA"]), ptr(glob["sB"]), h["m"], h["n"],
                                        h["k"], float(tau), float(safety), ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]),
                                        ptr(h["ws"]), h["ws"].numel(), self._stream()), "ozk_rule_finish")
-        self.engine.launches += 1
+        self.engine.launches += 2
         ctl, aux = self.engine._read_ctl(b)
         return ctl[0], ctl[1], ctl[2], ctl[3], aux
 

@@ -141,7 +141,7 @@ class OzakiCRT:
                                -1 if force_p is None else int(force_p), ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]),
                                ptr(b["ws_rule"]), b["ws_rule"].numel(), _stream_handle(stream))
         check(rc, "ozk_rule")
-        self.launches += 4
+        self.launches += 5
 
     def _stats_rule(self, A, B, b, tau, safety, inside, force_N=None, force_p=None):
         self.stats(A, B, b, inside)
@@ -301,7 +301,7 @@ class OzakiCRT:
         mark("start")
         g.replay()
         mark("stats+rule")
-        self.launches += 10
+        self.launches += 11
         ctl, _ = self._read_ctl(b)
         mark("host read")
         N, p, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
@@ -349,7 +349,7 @@ class OzakiCRT:
             e.record()
             events.append(("start", e))
         g.replay()
-        self.launches += 14
+        self.launches += 15
         torch.cuda.current_stream().synchronize()
         if events is not None:
             e = torch.cuda.Event(enable_timing=True)
@@ -452,7 +452,7 @@ class OzakiCRT:
                 C_h[r0:r1].copy_(C[r0:r1], non_blocking=True)
             # the next block's residues overwrite Ares / X: the copy only reads C, so nothing else to wait for
             r0 = r1
-        self.launches += 10 + 3 * (-(-m // rows)) + 1
+        self.launches += 11 + 3 * (-(-m // rows)) + 1
         cur.wait_stream(cs)
         cur.synchronize()
         return C_h, {"N": N, "p": p, "preq": preq, "blocks": -(-m // rows)}
