@@ -319,13 +319,17 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
     }
     // task coordinates, advanced by the grid stride without divisions in the loop:
     //   A: (v, lb) of the task's first chunk;  B: (vector group, l-block)
-    const int step = IS_B ? nwarps : nwarps * TC;
-    const int first = IS_B ? gwarp : gwarp * TC;
-    int cv = first / lblocks;
-    int clb = first - cv * lblocks;
+    //   B: consecutive warps take the two column groups of a pair (one 128-byte line of a row of B for TC = 8) at
+    //   the same l-block, then the pair moves along l; the warp count is even, so a warp keeps its half
+    const int step = IS_B ? (nwarps >> 1) : nwarps * TC;
+    const int first = IS_B ? (gwarp >> 1) : gwarp * TC;
+    const int bhalf = IS_B ? (gwarp & 1) : 0;
+    int tv = first / lblocks;
+    int clb = first - tv * lblocks;
     const int sv = step / lblocks;
     const int slb = step - sv * lblocks;
     for (int task = gwarp; task < ntasks; task += nwarps) {
+        const int cv = IS_B ? 2 * tv + bhalf : tv;
         double x[TC];
         int ag[TC];
         int cnt = TC;
@@ -386,9 +390,9 @@ __device__ __forceinline__ void split_tasks(const double* __restrict__ src, cons
             if (N <= 18) packed_tail<8>(wsm, kChunkBytes, tc1, N, cnt, o0, stride, plane_bytes);
             else packed_tail<4>(wsm, kChunkBytes, tc1, N, cnt, o0, stride, plane_bytes);
         }
-        cv += sv;
+        tv += sv;
         clb += slb;
-        if (clb >= lblocks) { clb -= lblocks; cv++; }
+        if (clb >= lblocks) { clb -= lblocks; tv++; }
     }
 }
 
