@@ -13,8 +13,9 @@
 // ok(p) is monotone in p, the smallest p is found per probe entry and p_req is their maximum.
 //
 // Kernels: rule_prep (1 block: nu, pv, forced / non-finite decisions, the top-32 selections), probe_partial
-// (split-K FP64 probe product), probe_reduce (partials added in block order), rule_final (1 block: p_req, N, p,
-// worst E/D).
+// (split-K FP64 probe product), probe_reduce (partials added in block order), rule_preq (one probe entry per
+// thread: p_req as the maximum of the per-entry p) and rule_final (one entry per thread: worst E/D; the last block
+// to finish decides N and p).
 #include <math.h>
 
 #include "ozk_common.cuh"
