@@ -294,9 +294,10 @@ def main():
     step_events = []
     products = 1
     if world > 1:
-        assert args.mode == "sampled", "--mode other than sampled is single-GPU"
+        assert args.mode in ("sampled", "certified"), "--mode config / persist are single-GPU"
         E = pkg.DistributedOzakiCRT(grid=(R, S))
-        call = lambda ev=None: E.run(A, B, C, force_N=forceN)  # noqa: E731
+        cert = args.mode == "certified"
+        call = lambda ev=None: E.run(A, B, C, force_N=forceN, certify=cert)  # noqa: E731
     else:
         E = pkg.OzakiCRT()
         call = lambda ev=None: E.run_fast(A, B, C, force_N=forceN, events=ev)  # noqa: E731

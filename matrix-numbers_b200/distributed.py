@@ -14,7 +14,11 @@ in this order on every rank:
   3. all_reduce(SUM) of the probe product D (96 x 96 doubles; each rank fills the entries whose probe row and probe
      column it holds, zeros elsewhere) -> every rank makes the same decision (N, p) from the same numbers;
 then each rank splits its A rows and B columns into residue planes, runs the N INT8 products and reconstructs its C
-block -- no further communication.  The result equals the single-GPU product bit for bit (same gamma, r, c, N, p;
+block -- no further communication.  With ``certify=True`` step 3 is the full-matrix certificate instead of the probe:
+each rank bounds every entry of its own block (the bound of entry (i, j) needs only row i's and column j's
+statistics and the global gamma), one all_reduce(MIN) of the blocks' minimum xmax (float64 bit patterns, which order
+like the values) gives the minimum over all of C, and one all_reduce(SUM) the uncertified count; every rank then makes
+the certified-mode decision from the same numbers.  The result equals the single-GPU product bit for bit (same gamma, r, c, N, p;
 the CRT stage is exact).
 
 Compute is delegated to an ``ops`` object: ``CudaOps`` (default) calls libozaki_b200.so on the rank's GPU; the CPU
@@ -129,6 +133,27 @@ class CudaOps:
         ctl, aux = self.engine._read_ctl(b)
         return ctl[0], ctl[1], ctl[2], ctl[3], aux
 
+    def certificate_block(self, A, B, st, tau, safety):
+        """This block's minimum xmax (float64 bit pattern as int64, -1 when no entry has D > 0) and its uncertified
+        entry count, both as 1-element device tensors (csrc/certificate.cu)."""
+        from .certificate import certificate_device
+        w = certificate_device(self.engine, A, B, st["gam"], st["r"], st["c"], st["sA"], st["sB"], tau, safety)
+        self._cert = w
+        return w["xmin"].view(torch.int64).clone(), w["unc"].clone()
+
+    def rule_certified(self, st, glob, m, n, k, xmin_bits):
+        """The certified-mode decision from the global minimum (``ozk_rule_certified``); (N, p, fallback, p_req)."""
+        b = st["_b"]
+        xm = xmin_bits.view(torch.float64)
+        check(self.lib.ozk_rule_certified(ptr(glob["nA"]), ptr(glob["nB"]), ptr(st["flag"]), m, n, k, ptr(xm),
+                                          ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]), self._stream()),
+              "ozk_rule_certified")
+        self.engine.launches += 1
+        ctl, aux = self.engine._read_ctl(b)
+        if int(self._cert["err"].item()):
+            raise _lib.OzkError(f"ozk_certificate: device error flag {int(self._cert['err'].item()):#x}")
+        return ctl[0], ctl[1], ctl[2], ctl[3]
+
     def core(self, A, B, st, N, p, C):
         rows, k = A.shape
         cols = B.shape[1]
@@ -188,7 +213,7 @@ class DistributedOzakiCRT:
         return parts[0:stride * count:stride].reshape(total)
 
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, safety=2.0,
-            config=None):
+            config=None, certify=False):
         if config is not None:
             force_N, force_p = int(config["N"]), config.get("p")
         rows, k = A.shape
@@ -210,6 +235,22 @@ class DistributedOzakiCRT:
             glob[x].copy_(self._gather(st[x], m, self.S, self.R))
         for x in ("c", "sB", "nB"):
             glob[x].copy_(self._gather(st[x], n, 1, self.S))
+        if certify and force_N is None:
+            # 3'. full-matrix certificate: minimum over the blocks, then the same decision everywhere
+            xb, unc = self.ops.certificate_block(A, B, st, tau, safety)
+            none = torch.full_like(xb, torch.iinfo(torch.int64).max)
+            xr = torch.where(xb == -1, none, xb)
+            dist.all_reduce(xr, op=dist.ReduceOp.MIN, group=self.group)
+            dist.all_reduce(unc, op=dist.ReduceOp.SUM, group=self.group)
+            xr = torch.where(xr == none, torch.full_like(xr, -1), xr)
+            N, p, fb, preq = self.ops.rule_certified(st, glob, m, n, k, xr)
+            if fb or N == 0:
+                self.ops.native(A, B, C)
+                return C, {"fallback": True, "preq": preq, "certified": True}
+            self.ops.core(A, B, st, N, p, C)
+            return C, {"N": N, "p": p, "preq": preq, "certified": True, "uncertified_entries": int(unc.item()),
+                       "rows": [row_begin, row_begin + rows], "cols": [col_begin, col_begin + cols],
+                       "grid": [self.R, self.S], "world": self.world}
         # 3. probe product summed over the blocks, then the same decision everywhere
         Ir, Jr = self._probe_sets(m, n, seed, A.device)
         h = self.ops.rule_prepare(st, glob, m, n, k, Ir, Jr, force_N, force_p)

@@ -341,6 +341,46 @@ def full_certificate(A, B, st, tau=2.0 ** -52, safety=2.0):
             "xmax": xmax}
 
 
+def certificate_xmin(A, B, st, tau=2.0 ** -52, safety=2.0):
+    """min xmax over the entries with D > 0 of ``full_certificate``'s bound (ozaki_engine.py:1542-1583) as the float64
+    bit pattern (int; -1 when no entry has D > 0), and the number of entries with D not > 0."""
+    cert = full_certificate(A, B, st, tau, safety)
+    mask = cert["D"] > 0
+    if not mask.any():
+        return -1, cert["uncertified"]
+    x = float(np.min(cert["xmax"][mask]))
+    return int(np.array([x], dtype=np.float64).view(np.int64)[0]), cert["uncertified"]
+
+
+def rule_certified(nA, nB, flag, k, xmin_bits):
+    """The plane-count decision from the certificate's minimum (the device rule of the certified mode):
+    p_req = ceil(-log2(xmin) + 1e-9) clamped to [1, 1000] (the reference's preq_full, :1570-1573), N = the smallest
+    plane count in [6, 32] whose pmax_bits reaches it (:1119-1139), fallback on a non-finite flag, no such N or
+    p_req > 249.  Returns (N, p, fallback, p_req)."""
+    nuA, nuB = math.sqrt(float(np.max(nA))), math.sqrt(float(np.max(nB)))
+    if xmin_bits == -1:
+        need = -1e30
+    else:
+        need = -math.log2(float(np.array([xmin_bits], dtype=np.int64).view(np.float64)[0]))
+    preq = int(min(max(math.ceil(need + 1e-9), 1), 1000))
+    N = next((t for t in range(6, NMAX + 1) if pmax_bits(t, nuA, nuB, k) >= preq), 0)
+    fb = bool(flag) or N == 0 or preq > 249
+    p = pmax_bits(N, nuA, nuB, k) if N else 0
+    return (0 if fb else N), p, fb, preq
+
+
+def run_certified(A, B, tau=2.0 ** -52, safety=2.0):
+    """The certified-mode product on the CPU: statistics, the full-matrix certificate's minimum, the certified rule,
+    then core at (N, p); (C, info) with C None on fallback."""
+    A, B = _c64(A), _c64(B)
+    st = stats(A, B, True)
+    xb, unc = certificate_xmin(A, B, st, tau, safety)
+    N, p, fb, preq = rule_certified(st["nA"], st["nB"], st["flag"], A.shape[1], xb)
+    if fb:
+        return None, {"fallback": True, "p_req": preq}
+    return core(A, B, st, N, p), {"N": N, "p": p, "p_req": preq, "uncertified": unc}
+
+
 def chain_exact(mats):
     """Exact product A_1 A_2 ... A_q of integer matrices as Python integers (numpy object arrays), the value an exact
     residue chain must reproduce (code/digit_gemm.py:1252-1291 models its cost: one INT8 GEMM per modulus per

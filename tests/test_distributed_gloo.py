@@ -79,6 +79,15 @@ class OracleOps:
             N = 0 if fb else N
         return N, p, fb, ru["p_req"], [ru["nuA"], ru["nuB"], ru["worst_ratio_E_over_D"], len(set(I)), len(set(J)), 0, 0, 0]
 
+    def certificate_block(self, A, B, st, tau, safety):
+        xb, unc = self.O.certificate_xmin(A.numpy(), B.numpy(), st["_np"], tau, safety)
+        return torch.tensor([xb], dtype=torch.int64), torch.tensor([unc], dtype=torch.int64)
+
+    def rule_certified(self, st, glob, m, n, k, xmin_bits):
+        N, p, fb, preq = self.O.rule_certified(glob["nA"].numpy(), glob["nB"].numpy(), int(st["flag"][0]), k,
+                                               int(xmin_bits[0]))
+        return N, p, int(fb), preq
+
     def core(self, A, B, st, N, p, C):
         C.copy_(torch.from_numpy(self.O.core(A.numpy(), B.numpy(), st["_np"], N, p)))
         return C
@@ -88,7 +97,7 @@ class OracleOps:
         return C
 
 
-GRIDS = {"ok": (2, 1), "cols": (1, 2), "grid4": (2, 2)}
+GRIDS = {"ok": (2, 1), "cols": (1, 2), "grid4": (2, 2), "cert": (2, 1), "cert4": (2, 2)}
 
 
 def _worker(rank, world, port, outdir, mode):
@@ -116,7 +125,7 @@ def _worker(rank, world, port, outdir, mode):
         D = DistributedOzakiCRT(ops=OracleOps(O), grid=(R, S))
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure on rank 1 before the first collective")
-        C, info = D.run(Al, Bt)
+        C, info = D.run(Al, Bt, certify=mode.startswith("cert"))
         C2, info2 = D.run(Al, Bt, force_N=22)
         np.save(os.path.join(outdir, f"C_{rank}.npy"), C.numpy())
         np.save(os.path.join(outdir, f"C22_{rank}.npy"), C2.numpy())
@@ -161,6 +170,26 @@ def test_blocks_equal_single_process(oracle, tmp_path, pkg, mode, world):
     C22ref, i22 = oracle.run(A, B, force_N=22)
     np.testing.assert_array_equal(assemble("C22").view(np.uint64), C22ref.view(np.uint64))
     assert infos[0][3:] == (22, i22["p"])
+
+
+@pytest.mark.parametrize("mode,world", [("cert", 2), ("cert4", 4)])
+def test_certified_blocks_equal_single_process(oracle, tmp_path, pkg, mode, world):
+    """Certified mode over the grid: the blocks' minimum bound, reduced with MIN, gives the same decision and the
+    same C as the whole-matrix certificate of the single-process oracle."""
+    alive = _spawn(world, mode, tmp_path)
+    assert not any(alive)
+    errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    R, S = GRIDS[mode]
+    A, B = pkg.make_inputs(128, 256, 128, 2.0, seed=31)
+    C = np.concatenate([np.concatenate([np.load(os.path.join(tmp_path, f"C_{a * S + b}.npy")) for b in range(S)], axis=1)
+                        for a in range(R)])
+    Cref, iref = oracle.run_certified(A, B)
+    assert Cref is not None
+    np.testing.assert_array_equal(C.view(np.uint64), Cref.view(np.uint64))
+    infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(world)]
+    assert all(i == infos[0] for i in infos)
+    assert infos[0][:3] == (iref["N"], iref["p"], iref["p_req"])
 
 
 def test_failed_rank_ends_peers_collective_with_error(tmp_path):

@@ -36,6 +36,10 @@ def test_distributed_one_rank_nccl(pkg, engine):
         C2, i2 = D.run(Ad, Bd, force_N=20)
         C2r, _ = engine.run(Ad, Bd, force_N=20)
         assert i2["N"] == 20 and torch.equal(C2, C2r)
+        C3, i3c = D.run(Ad, Bd, certify=True)
+        C3r, i3r = engine.run(Ad, Bd, certify=True)
+        assert i3c["certified"] and (i3c["N"], i3c["p"], i3c["preq"]) == (i3r["N"], i3r["p"], i3r["p_req"])
+        assert i3c["uncertified_entries"] == i3r["uncertified_entries"] and torch.equal(C3, C3r)
         Bn = Bd.clone()
         Bn[3, 4] = float("nan")
         _, i3 = D.run(Ad, Bn)
