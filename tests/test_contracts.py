@@ -76,3 +76,30 @@ def test_timed_path_fallback_flag(pkg, engine):
     An[3, 5] = float("nan")
     _, i_nan = engine.run(An, Bd, C=Cx, graph=True)
     assert not i_ok.get("fallback") and i_nan.get("fallback")
+
+
+def test_error_conventions(pkg, engine):
+    """The reference's error conventions (ozaki_engine.py:1315-1316 asserts; a RuntimeError from the GPU layer):
+    shape violations and wrong dtypes raise AssertionError before any launch, eagerly and on the timed path;
+    zero-sized problems are rejected by the C ABI's argument checks as a RuntimeError."""
+    import torch
+    A, B = pkg.make_inputs(64, 128, 64, 0.5, seed=4)
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    bad = [(Ad[:, :120].contiguous(), Bd[:120]),             # k % 32 != 0
+           (Ad, Bd[:, :48].contiguous()),                     # n % 32 != 0
+           (Ad[:62].contiguous(), Bd),                        # m % 4 != 0
+           (Ad.float(), Bd),                                  # not float64
+           (Ad.t(), Bd),                                      # not contiguous (and k differs)
+           (Ad, Bd[:96])]                                     # inner dimensions differ
+    for a, b in bad:
+        with pytest.raises(AssertionError):
+            engine.run(a, b)
+        with pytest.raises(AssertionError):
+            engine.run(a, b, C=torch.empty(a.shape[0], b.shape[1], dtype=torch.float64, device="cuda"), graph=True)
+    with pytest.raises(AssertionError):
+        engine.run(Ad, Bd, C=torch.empty(64, 32, dtype=torch.float64, device="cuda"))   # C of the wrong shape
+    with pytest.raises(RuntimeError):
+        engine.run(Ad[:0], Bd)                                                        # m = 0
+    C, info = engine.run(Ad, Bd)                                 # the engine is still usable afterwards
+    Cr, _ = engine.run(Ad, Bd)
+    assert torch.equal(C, Cr)
