@@ -457,6 +457,106 @@ class OzakiCRT:
         cur.synchronize()
         return C_h, {"N": N, "p": p, "preq": preq, "blocks": -(-m // rows)}
 
+    def run_host_many(self, jobs, tau=2.0 ** -52, safety=2.0, inside=True, force_N=None, force_p=None, blocks=4):
+        """A stream of host-buffer products: ``jobs`` is a list of (A_h, B_h, C_h) pinned float64 CPU tensors of one
+        shape (C_h None to allocate); returns [(C_h, info), ...], each equal to ``run_host``'s bit for bit.
+
+        A single call cannot overlap its input copies with its products (the statistics need all of A and B), but a
+        stream can: the device holds two input slots, and the H2D copies of job i + 1 run on their own stream while
+        job i computes and its row blocks of C go back on a third stream (PCIe carries both directions at once).
+        Job i + 1's copies are issued before job i's one blocking read of (N, p)."""
+        if not jobs:
+            return []
+        m, k = jobs[0][0].shape
+        n = jobs[0][1].shape[1]
+        for A_h, B_h, _ in jobs:
+            assert A_h.dtype == torch.float64 and B_h.dtype == torch.float64
+            assert tuple(A_h.shape) == (m, k) and tuple(B_h.shape) == (k, n), "all jobs must have one shape"
+        io = self.__dict__.setdefault("_host_many", {})
+        dv = io.get((m, n, k))
+        if dv is None:
+            io.clear()
+            dv = {"slots": [{x: torch.empty(sh, dtype=torch.float64, device=DEV)
+                             for x, sh in (("A", (m, k)), ("B", (k, n)), ("C", (m, n)))} for _ in range(2)],
+                  "cin": torch.cuda.Stream(), "cout": torch.cuda.Stream()}
+            io[(m, n, k)] = dv
+        slots, cin, cout = dv["slots"], dv["cin"], dv["cout"]
+        self._shape_check(slots[0]["A"], slots[0]["B"], slots[0]["C"])
+        cur = torch.cuda.current_stream()
+        cin.wait_stream(cur)
+        cout.wait_stream(cur)
+        in_done = [torch.cuda.Event(), torch.cuda.Event()]
+        used = [None, None]                                   # (compute done, D2H done) events of the slot's last job
+        outs = [C_h if C_h is not None else torch.empty((m, n), dtype=torch.float64, pin_memory=True)
+                for _, _, C_h in jobs]
+
+        def h2d(i):
+            s = i % 2
+            if used[s] is not None:
+                cin.wait_event(used[s][0])                    # the slot's previous job has read its A and B
+            with torch.cuda.stream(cin):
+                slots[s]["A"].copy_(jobs[i][0], non_blocking=True)
+                slots[s]["B"].copy_(jobs[i][1], non_blocking=True)
+            in_done[s].record(cin)
+
+        h2d(0)
+        results = []
+        rows = ((-(-m // blocks) + 127) // 128) * 128         # whole 128-row tiles per block
+        for i in range(len(jobs)):
+            s = i % 2
+            A, B, C, C_h = slots[s]["A"], slots[s]["B"], slots[s]["C"], outs[i]
+            if i + 1 < len(jobs):
+                h2d(i + 1)
+            cur.wait_event(in_done[s])
+            if used[s] is not None:
+                cur.wait_event(used[s][1])                    # C of the slot's previous job has been copied out
+            b = self.buffers(m, n, k, 20 if force_N is None else max(20, int(force_N)))
+            self._stats_rule(A, B, b, tau, safety, inside, force_N, force_p)
+            ctl, _ = self._read_ctl(b)
+            N, p, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
+            if not (fb or N == 0) and b["N"] < N:
+                b = self.buffers(m, n, k, N)
+                self._stats_rule(A, B, b, tau, safety, inside, force_N, force_p)
+            if fb or N == 0:
+                torch.matmul(A, B, out=C)
+                cdone = torch.cuda.Event()
+                cdone.record(cur)
+                cout.wait_event(cdone)
+                with torch.cuda.stream(cout):
+                    C_h.copy_(C, non_blocking=True)
+                info = {"fallback": True, "preq": preq}
+            else:
+                st = _stream_handle()
+                check(self.lib.ozk_split_b(ptr(B), ptr(b["c"]), ptr(b["gam"]), ptr(b["pdev"]), k, n, N, ptr(b["Bres"]),
+                                           st), "ozk_split_b")
+                r0 = 0
+                while r0 < m:
+                    r1 = min(m, r0 + rows)
+                    mb = r1 - r0
+                    check(self.lib.ozk_split_a(ptr(A[r0:r1]), ptr(b["r"][r0:r1]), ptr(b["gam"]), ptr(b["pdev"]), mb, k,
+                                               N, ptr(b["Ares"]), st), "ozk_split_a")
+                    check(self.lib.ozk_gemm_residues(ptr(b["Ares"]), ptr(b["Bres"]), mb, n, k, N, ptr(b["X"]),
+                                                     ptr(b["err"]), st), "ozk_gemm_residues")
+                    check(self.lib.ozk_reconstruct(ptr(b["X"]), ptr(b["r"][r0:r1]), ptr(b["c"]), ptr(b["pdev"]), mb, n,
+                                                   N, ptr(C[r0:r1]), st), "ozk_reconstruct")
+                    done = torch.cuda.Event()
+                    done.record(cur)
+                    cout.wait_event(done)
+                    with torch.cuda.stream(cout):
+                        C_h[r0:r1].copy_(C[r0:r1], non_blocking=True)
+                    r0 = r1
+                self.launches += 11 + 3 * (-(-m // rows)) + 1
+                info = {"N": N, "p": p, "preq": preq, "blocks": -(-m // rows)}
+            cdone, odone = torch.cuda.Event(), torch.cuda.Event()
+            cdone.record(cur)
+            odone.record(cout)
+            used[s] = (cdone, odone)
+            results.append((C_h, info))
+        cur.wait_stream(cout)
+        cur.wait_stream(cin)
+        cur.synchronize()
+        return results
+
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, graph=False, prof=None, seed=0, config=None,
             force_p=None, certify=False):
         """C = A B in emulated FP64; returns (C, info).  ``config`` ({'N':.., 'p':..}, e.g. from pick_config) overrides
