@@ -265,4 +265,66 @@ class DistributedOzakiCRT:
                    "cols": [col_begin, col_begin + cols], "grid": [self.R, self.S], "world": self.world}
 
 
+    def run_host_many(self, jobs, **kw):
+        """A stream of host-buffer products on this rank: ``jobs`` is a list of (A_rows_h, B_cols_h, C_block_h)
+        pinned float64 CPU tensors of one shape (C_block_h None to allocate), the same list length and keyword
+        arguments (those of ``run``) on every rank.  Two device slots: the H2D copies of job i + 1 run on their own
+        stream while job i computes (its collectives included) and its C block goes back on a third stream.
+        Returns [(C_block_h, info), ...]; each equals a ``run`` on the same blocks bit for bit."""
+        if not jobs:
+            return []
+        rows, k = jobs[0][0].shape
+        cols = jobs[0][1].shape[1]
+        dev = torch.device("cuda", torch.cuda.current_device())
+        key = (rows, cols, k)
+        io = self.__dict__.setdefault("_host_many", {})
+        dv = io.get(key)
+        if dv is None:
+            io.clear()
+            dv = {"slots": [{x: torch.empty(sh, dtype=torch.float64, device=dev)
+                             for x, sh in (("A", (rows, k)), ("B", (k, cols)), ("C", (rows, cols)))} for _ in range(2)],
+                  "cin": torch.cuda.Stream(), "cout": torch.cuda.Stream()}
+            io[key] = dv
+        slots, cin, cout = dv["slots"], dv["cin"], dv["cout"]
+        cur = torch.cuda.current_stream()
+        cin.wait_stream(cur)
+        cout.wait_stream(cur)
+        in_done = [torch.cuda.Event(), torch.cuda.Event()]
+        used = [None, None]
+        outs = [C_h if C_h is not None else torch.empty((rows, cols), dtype=torch.float64, pin_memory=True)
+                for _, _, C_h in jobs]
+
+        def h2d(i):
+            s = i % 2
+            if used[s] is not None:
+                cin.wait_event(used[s][0])
+            with torch.cuda.stream(cin):
+                slots[s]["A"].copy_(jobs[i][0], non_blocking=True)
+                slots[s]["B"].copy_(jobs[i][1], non_blocking=True)
+            in_done[s].record(cin)
+
+        h2d(0)
+        results = []
+        for i in range(len(jobs)):
+            s = i % 2
+            if i + 1 < len(jobs):
+                h2d(i + 1)
+            cur.wait_event(in_done[s])
+            if used[s] is not None:
+                cur.wait_event(used[s][1])
+            C, info = self.run(slots[s]["A"], slots[s]["B"], slots[s]["C"], **kw)
+            cdone, odone = torch.cuda.Event(), torch.cuda.Event()
+            cdone.record(cur)
+            cout.wait_event(cdone)
+            with torch.cuda.stream(cout):
+                outs[i].copy_(C, non_blocking=True)
+            odone.record(cout)
+            used[s] = (cdone, odone)
+            results.append((outs[i], info))
+        cur.wait_stream(cout)
+        cur.wait_stream(cin)
+        cur.synchronize()
+        return results
+
+
 __all__ = ["DistributedOzakiCRT", "CudaOps", "default_grid", "_lib"]

@@ -40,6 +40,19 @@ def test_distributed_one_rank_nccl(pkg, engine):
         C3r, i3r = engine.run(Ad, Bd, certify=True)
         assert i3c["certified"] and (i3c["N"], i3c["p"], i3c["preq"]) == (i3r["N"], i3r["p"], i3r["p_req"])
         assert i3c["uncertified_entries"] == i3r["uncertified_entries"] and torch.equal(C3, C3r)
+        jobs, want = [], []
+        for seed in range(3):
+            A2, B2 = pkg.make_inputs(256, 512, 384, 1.0 + seed, seed=20 + seed)
+            jobs.append((torch.from_numpy(A2).pin_memory(), torch.from_numpy(B2).pin_memory(), None))
+            want.append(D.run(torch.from_numpy(A2).cuda(), torch.from_numpy(B2).cuda(), certify=seed == 1))
+        got = D.run_host_many(jobs[:1], certify=False) + D.run_host_many(jobs[1:2], certify=True) + \
+            D.run_host_many(jobs[2:], certify=False)
+        for (Cg, ig), (Cw, iw) in zip(got, want):
+            assert (ig["N"], ig["p"]) == (iw["N"], iw["p"])
+            assert torch.equal(Cg, Cw.cpu())
+        many = D.run_host_many([jobs[0], jobs[2], jobs[0]])
+        assert torch.equal(many[0][0], want[0][0].cpu()) and torch.equal(many[1][0], want[2][0].cpu())
+        assert torch.equal(many[2][0], want[0][0].cpu())
         Bn = Bd.clone()
         Bn[3, 4] = float("nan")
         _, i3 = D.run(Ad, Bn)
