@@ -76,12 +76,11 @@ __device__ __forceinline__ double hard_value(int e, double s, int k) {
     return s > 0.0 ? __ddiv_rn(__dmul_rn(ldexp(1.0, e), (double)k), s) : 0.0;
 }
 
-// Select the `cnt` (<= 32) first indices of the stable descending order of the values hv[0..len) ("larger value
-// first, then lower index"); writes them to out[0..cnt).  The values are hard values (>= 0, +inf possible, never
-// NaN), so their bit patterns order like the values.  Each warp keeps the sorted top-32 of its contiguous segment,
-// one entry per lane (a 32-element bitonic sort per chunk of 32, then a bitonic merge with the running list); the 32
-// lists are merged pairwise in 5 rounds through shared memory.  Ties between values are broken by index, so the
-// result is the same set and order as a stable sort.
+// Stable top-32 selection ("larger value first, then lower index"): the values are hard values (>= 0, +inf possible,
+// never NaN), so their bit patterns order like the values.  A warp keeps the sorted top-32 of its segment, one entry
+// per lane (a 32-element bitonic sort per chunk of 32, then a bitonic merge with the running list); the warps' lists
+// are merged pairwise through shared memory.  Ties between values are broken by index, so the result is the same set
+// and order as a stable sort.
 struct KeyIdx { unsigned long long key; int idx; };
 
 __device__ __forceinline__ bool kbefore(unsigned long long k, int i, unsigned long long bk, int bi) {
@@ -121,17 +120,21 @@ __device__ __forceinline__ void merge_lists(unsigned long long& key, int& idx, u
 
 constexpr int kNoIdx = 0x7fffffff;
 
-__device__ void top_hard(const double* __restrict__ hv, int len, int cnt, int* out, KeyIdx* lists) {
+// The stable top-32 of `len` (key, index) pairs given by ld(x) = (key, idx) for x in [0, len): each warp keeps the
+// sorted top-32 of its contiguous segment, the warps' lists are merged pairwise in shared memory.  On return warp 0
+// holds the result, entry `lane` in (key, idx) (idx kNoIdx where fewer than 32 pairs exist).
+template <typename Loader>
+__device__ void top32(Loader ld, int len, KeyIdx* lists, unsigned long long& key, int& idx) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int seg = (len + nw - 1) / nw;
     const int b0 = w * seg, b1 = min(len, b0 + seg);
-    unsigned long long key = 0ULL;
-    int idx = kNoIdx;
+    key = 0ULL;
+    idx = kNoIdx;
     for (int c0 = b0; c0 < b1; c0 += 32) {
         const int x = c0 + lane;
         unsigned long long ck = 0ULL;
         int ci = kNoIdx;
-        if (x < b1) { ck = (unsigned long long)__double_as_longlong(hv[x]); ci = x; }
+        if (x < b1) ld(x, ck, ci);
         bitonic_sort_desc(ck, ci);
         merge_lists(key, idx, ck, ci);
     }
@@ -146,8 +149,40 @@ __device__ void top_hard(const double* __restrict__ hv, int len, int cnt, int* o
         if (w < half) lists[w * 32 + lane] = KeyIdx{key, idx};
         __syncthreads();
     }
-    if (w == 0 && lane < cnt) out[lane] = idx == kNoIdx ? 0 : idx;
-    __syncthreads();
+}
+
+// Hard-index candidates: block b < nbr takes rows [b kHardSeg, (b + 1) kHardSeg) of the hard values 2^r_i k / sA_i,
+// the other blocks the columns; each writes the stable top-32 of its segment as (key, global index) pairs.  The
+// global top-32 of a side is the top-32 of its blocks' candidates (every member is in its own segment's top-32, and
+// the pairs keep the original index for the ties), merged by rule_prep_kernel.
+constexpr int kHardSeg = 256;
+constexpr int kHardThreads = 256;
+__host__ __device__ inline int hard_blocks(int len) { return (len + kHardSeg - 1) / kHardSeg; }
+
+__global__ void __launch_bounds__(kHardThreads) hard_cand_kernel(const int32_t* __restrict__ r,
+                                                                 const int32_t* __restrict__ c,
+                                                                 const double* __restrict__ sA,
+                                                                 const double* __restrict__ sB, int m, int n, int k,
+                                                                 unsigned long long* __restrict__ ckey,
+                                                                 int* __restrict__ cidx) {
+    __shared__ KeyIdx lists[kHardThreads];
+    const int nbr = hard_blocks(m);
+    const bool rows = (int)blockIdx.x < nbr;
+    const int b = rows ? (int)blockIdx.x : (int)blockIdx.x - nbr;
+    const int base = b * kHardSeg;
+    const int len = min(kHardSeg, (rows ? m : n) - base);
+    const int32_t* e = rows ? r : c;
+    const double* sv = rows ? sA : sB;
+    unsigned long long key;
+    int idx;
+    top32([&](int x, unsigned long long& ck, int& ci) {
+        ck = (unsigned long long)__double_as_longlong(hard_value(e[base + x], sv[base + x], k));
+        ci = base + x;
+    }, len, lists, key, idx);
+    if (threadIdx.x < 32) {
+        ckey[(size_t)blockIdx.x * 32 + threadIdx.x] = key;
+        cidx[(size_t)blockIdx.x * 32 + threadIdx.x] = idx;
+    }
 }
 
 __device__ double block_max(double v, double* sm) {
@@ -171,7 +206,8 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
     const double* __restrict__ nA, const double* __restrict__ sB, const double* __restrict__ nB,
     const int32_t* __restrict__ flag, const int64_t* __restrict__ Ir, int nIr, const int64_t* __restrict__ Jr, int nJr,
     int m, int n, int k, int force_N, int force_p, MTable mt, RuleCtl* __restrict__ ctl, int32_t* __restrict__ dec,
-    int32_t* __restrict__ p_dev, double* __restrict__ aux, double* __restrict__ hv) {
+    int32_t* __restrict__ p_dev, double* __restrict__ aux, const unsigned long long* __restrict__ ckey,
+    const int* __restrict__ cidx) {
     __shared__ double smv[32];
     // max nA, max nB (order-independent)
     double mA = 0.0, mB = 0.0;
@@ -214,13 +250,17 @@ __global__ void __launch_bounds__(kPrepThreads) rule_prep_kernel(
     // caller-supplied probe indices are clamped into range (an out-of-range index must not be dereferenced)
     for (int x = threadIdx.x; x < nIr; x += blockDim.x) ctl->I[x] = (Ir[x] >= 0 && Ir[x] < m) ? (int)Ir[x] : 0;
     for (int x = threadIdx.x; x < nJr; x += blockDim.x) ctl->J[x] = (Jr[x] >= 0 && Jr[x] < n) ? (int)Jr[x] : 0;
-    // the hard values 2^e k / s, computed once into the workspace, then the stable top-32 of rows and of columns
-    for (int x = threadIdx.x; x < m; x += blockDim.x) hv[x] = hard_value(r[x], sA[x], k);
-    for (int x = threadIdx.x; x < n; x += blockDim.x) hv[m + x] = hard_value(c[x], sB[x], k);
-    __syncthreads();
+    // the stable top-32 of rows and of columns from the blocks' candidates (hard_cand_kernel)
     __shared__ KeyIdx lists[kPrepThreads];
-    top_hard(hv, m, hr, ctl->I + nIr, lists);
-    top_hard(hv + m, n, hc, ctl->J + nJr, lists);
+    const int nbr = hard_blocks(m), nbc = hard_blocks(n);
+    unsigned long long key;
+    int idx;
+    top32([&](int x, unsigned long long& ck, int& ci) { ck = ckey[x]; ci = cidx[x]; }, nbr * 32, lists, key, idx);
+    if (threadIdx.x < hr) ctl->I[nIr + threadIdx.x] = idx == kNoIdx ? 0 : idx;
+    __syncthreads();
+    top32([&](int x, unsigned long long& ck, int& ci) { ck = ckey[(size_t)nbr * 32 + x]; ci = cidx[(size_t)nbr * 32 + x]; },
+          nbc * 32, lists, key, idx);
+    if (threadIdx.x < hc) ctl->J[nJr + threadIdx.x] = idx == kNoIdx ? 0 : idx;
 }
 
 // split-K probe product: partial[b][a][j] = sum over this block's contraction tiles of |A_I[a] l| |B_l J[j]|
@@ -283,15 +323,26 @@ __global__ void __launch_bounds__(kProbeThreads) probe_partial_kernel(const doub
         for (int v = 0; v < 6; v++) out[(a0 + u) * kProbeMax + b0 + v] = acc[u][v];
 }
 
-// D[a][b] = sum of the per-block partials in block order (fixed order: bitwise reproducible)
-__global__ void probe_reduce_kernel(const double* __restrict__ partial, int nblocks, const RuleCtl* __restrict__ ctl,
-                                    double* __restrict__ D) {
+// D[a][b] = sum of the per-block partials: one block per 32 entries (lane = entry, coalesced), 8 warps over the
+// partials (warp w: partials w, w + 8, ...), the warps' sums added in warp order (fixed order: bitwise reproducible)
+constexpr int kReduceWarps = 8;
+__global__ void __launch_bounds__(kReduceWarps * 32) probe_reduce_kernel(const double* __restrict__ partial,
+                                                                         int nblocks, const RuleCtl* __restrict__ ctl,
+                                                                         double* __restrict__ D) {
     if (ctl->done) return;
-    const int e = blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= kProbeMax * kProbeMax) return;
+    __shared__ double sm[kReduceWarps][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int e = blockIdx.x * 32 + lane;              // kProbeMax^2 is a multiple of 32
     double s = 0.0;
-    for (int h = 0; h < nblocks; h++) s += partial[(size_t)h * kProbeMax * kProbeMax + e];
-    D[e] = s;
+    for (int h = w; h < nblocks; h += kReduceWarps) s += partial[(size_t)h * kProbeMax * kProbeMax + e];
+    sm[w][lane] = s;
+    __syncthreads();
+    if (w == 0) {
+        double t = 0.0;
+#pragma unroll
+        for (int u = 0; u < kReduceWarps; u++) t += sm[u][lane];
+        D[e] = t;
+    }
 }
 
 struct EntryTerms { double F1, F2, rhs; };   // rhs = tau * D
@@ -420,12 +471,16 @@ int probe_blocks(int k) {
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // about four contraction tiles per block (each block writes a 96 x 96 partial) once there are enough tiles for
+    // 64 blocks, one tile per block below that (short k: latency-bound gathers), at most two blocks per SM
     const int tiles = (k + kProbeK - 1) / kProbeK;
-    return max(1, min(tiles, 2 * sms));
+    return max(1, min(min(tiles, 2 * sms), max((tiles + 3) / 4, 64)));
 }
 
 size_t ctl_bytes() { return (sizeof(RuleCtl) + 255) & ~(size_t)255; }
-size_t hard_bytes(int m, int n) { return ((size_t)(m + n) * sizeof(double) + 255) & ~(size_t)255; }
+size_t cand_count(int m, int n) { return (size_t)(hard_blocks(m) + hard_blocks(n)) * 32; }
+// hard-index candidates: keys (8 bytes) then indices (4 bytes)
+size_t hard_bytes(int m, int n) { return ((cand_count(m, n) * 12) + 255) & ~(size_t)255; }
 
 // The rule driven by the full-matrix certificate (min xmax over all entries, csrc/certificate.cu) instead of the
 // probe: p_req = ceil(-log2(xmin) + 1e-9) clamped to [1, 1000] as the sampled rule clamps it, N = the smallest plane
@@ -489,10 +544,15 @@ extern "C" int ozk_rule_prepare(const int32_t* r, const int32_t* c, const double
     MTable mt;
     for (int N = 0; N <= OZK_NMAX; N++) mt.M[N] = N ? ozk_modulus_product(N) : 1.0;
     RuleCtl* ctl = static_cast<RuleCtl*>(workspace);
-    double* hv = reinterpret_cast<double*>(static_cast<char*>(workspace) + ctl_bytes());
+    unsigned long long* ckey = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + ctl_bytes());
+    int* cidx = reinterpret_cast<int*>(ckey + cand_count(m, n));
+    if (force_N == 0) {
+        hard_cand_kernel<<<hard_blocks(m) + hard_blocks(n), kHardThreads, 0, st>>>(r, c, sA, sB, m, n, k, ckey, cidx);
+        OZK_CHECK_LAUNCH();
+    }
     rule_prep_kernel<<<1, kPrepThreads, 0, st>>>(r, c, sA, nA, sB, nB, flag, probe_rows, n_probe_rows, probe_cols,
                                                  n_probe_cols, m, n, k, force_N, force_N > 0 ? force_p : -1, mt, ctl, dec,
-                                                 p_dev, aux, hv);
+                                                 p_dev, aux, ckey, cidx);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }
@@ -511,7 +571,7 @@ extern "C" int ozk_rule_probe_block(const double* A_rows, const double* B_cols, 
     probe_partial_kernel<<<nb, kProbeThreads, 0, st>>>(A_rows, B_cols, row_begin, rows, col_begin, cols, k, ctl, partial);
     OZK_CHECK_LAUNCH();
     double* D = partial + (size_t)nb * kProbeMax * kProbeMax;
-    probe_reduce_kernel<<<(kProbeMax * kProbeMax + 255) / 256, 256, 0, st>>>(partial, nb, ctl, D);
+    probe_reduce_kernel<<<kProbeMax * kProbeMax / 32, kReduceWarps * 32, 0, st>>>(partial, nb, ctl, D);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }

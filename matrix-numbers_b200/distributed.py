@@ -113,7 +113,7 @@ class CudaOps:
                                         ptr(Jr), Jr.numel(), int(force_N or 0), -1 if force_p is None else int(force_p),
                                         ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]), ptr(ws), ws.numel(),
                                         self._stream()), "ozk_rule_prepare")
-        self.engine.launches += 1
+        self.engine.launches += 1 if force_N else 2
         return {"ws": ws, "b": b, "m": m, "n": n, "k": k}
 
     def rule_probe(self, h, A, B, row_begin, col_begin):

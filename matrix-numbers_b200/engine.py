@@ -141,7 +141,7 @@ class OzakiCRT:
                                -1 if force_p is None else int(force_p), ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]),
                                ptr(b["ws_rule"]), b["ws_rule"].numel(), _stream_handle(stream))
         check(rc, "ozk_rule")
-        self.launches += 5
+        self.launches += 5 if force_N else 6
 
     def _stats_rule(self, A, B, b, tau, safety, inside, force_N=None, force_p=None):
         self.stats(A, B, b, inside)
@@ -301,7 +301,7 @@ class OzakiCRT:
         mark("start")
         g.replay()
         mark("stats+rule")
-        self.launches += 11
+        self.launches += 11 if force_N else 12
         ctl, _ = self._read_ctl(b)
         mark("host read")
         N, p, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
@@ -452,7 +452,7 @@ class OzakiCRT:
                 C_h[r0:r1].copy_(C[r0:r1], non_blocking=True)
             # the next block's residues overwrite Ares / X: the copy only reads C, so nothing else to wait for
             r0 = r1
-        self.launches += 11 + 3 * (-(-m // rows)) + 1
+        self.launches += (11 if force_N else 12) + 3 * (-(-m // rows)) + 1
         cur.wait_stream(cs)
         cur.synchronize()
         return C_h, {"N": N, "p": p, "preq": preq, "blocks": -(-m // rows)}
@@ -545,7 +545,7 @@ class OzakiCRT:
                     with torch.cuda.stream(cout):
                         C_h[r0:r1].copy_(C[r0:r1], non_blocking=True)
                     r0 = r1
-                self.launches += 11 + 3 * (-(-m // rows)) + 1
+                self.launches += (11 if force_N else 12) + 3 * (-(-m // rows)) + 1
                 info = {"N": N, "p": p, "preq": preq, "blocks": -(-m // rows)}
             cdone, odone = torch.cuda.Event(), torch.cuda.Event()
             cdone.record(cur)
