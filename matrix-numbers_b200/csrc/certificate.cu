@@ -15,7 +15,11 @@
 // shared memory); the product is a persistent tcgen05.mma kind::f16 kernel (128 x 256 tiles, 4-stage TMA ring with
 // 128-byte swizzle, FP32 accumulators double-buffered in TMEM), whose 8 epilogue warps evaluate the bound for every
 // entry straight out of TMEM and reduce min xmax / the uncertified count per warp, so the m x n matrix D never
-// reaches HBM (an optional debug output writes D).  Waits are bounded; no cluster multicast.
+// reaches HBM (an optional debug output writes D).  Only the minimum matters, so an entry is skipped once a lower
+// bound of its xmax cannot beat the running minimum (published across CTAs after every tile): first a
+// division-free test against per-tile thresholds, then the formula with approximate reciprocals, both with a 2^-8
+// margin; the exact reference formula runs only for the entries near the minimum.  Waits are bounded; no cluster
+// multicast.
 #include <cuda.h>
 #include <cuda_fp16.h>
 

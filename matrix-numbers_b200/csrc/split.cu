@@ -17,7 +17,9 @@
 // (m_t / 2 for m_t = 256, (m_t - 1) / 2 for odd m_t) and onto 0: q = floor((s + h) / m_t) is one multiply-high by
 // ceil(2^32 / m_t) (exact for s + h < 2^24), and the low byte of s - m_t q is the symmetric residue -- two integer
 // instructions per residue, no per-modulus digit sums and no sign handling.  The element -> MMA column assignment
-// gives each thread 8 consecutive elements of a modulus: one 8-byte store.
+// gives each thread 8 consecutive elements of a modulus: one 8-byte store.  Moduli beyond the first 16 take a second
+// 16-modulus row tile, except for 16 < N <= 20 with 16-byte strings, where the rows of one tile are (chunk, modulus)
+// pairs of several chunks (packed_tail) so that few rows stay idle.
 #include "ozk_common.cuh"
 
 namespace {
