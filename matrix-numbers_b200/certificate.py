@@ -42,7 +42,7 @@ def certificate_device(E, A, B, gam, r, c, sA, sB, tau=2.0 ** -52, safety=2.0, D
     check(E.lib.ozk_certificate(ptr(A), ptr(B), m, n, k, ptr(gam), ptr(r), ptr(c), ptr(sA), ptr(sB), float(tau),
                                 float(safety), ptr(w["xmin"]), ptr(w["unc"]), 0 if D_out is None else ptr(D_out),
                                 ptr(w["err"]), ptr(w["ws"]), w["ws"].numel(), _stream_handle(stream)), "ozk_certificate")
-    E.launches += 3
+    E.launches += 4                                   # 2^gamma tables, FP16 A and B, the product
     return w
 
 

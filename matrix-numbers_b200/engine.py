@@ -301,7 +301,8 @@ class OzakiCRT:
         mark("start")
         g.replay()
         mark("stats+rule")
-        self.launches += 11 if force_N else 12
+        # statistics (6) + sampled rule (6, 5 when N is forced) or certificate (4) + certified rule (1)
+        self.launches += 11 if (force_N or certify) else 12
         ctl, _ = self._read_ctl(b)
         mark("host read")
         N, p, fb, preq = ctl[0], ctl[1], ctl[2], ctl[3]
