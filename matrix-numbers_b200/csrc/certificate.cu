@@ -41,7 +41,8 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
 constexpr uint32_t IDESC = umma_idesc_f16_f32(BM, BN);
 constexpr int NUM_BARS = 2 * STAGES + 5;
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int COLSTAGE_DOUBLES = 3 * 32;          // per epilogue warp: 2^c_j, g_j, sB_j of its 32 columns
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256 + (size_t)EPI_WARPS * COLSTAGE_DOUBLES * 8;
 constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;
 constexpr unsigned long long kEmpty = 0xFFFFFFFFFFFFFFFFull;   // "no certified entry" (above every double's bits)
 
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    double* colstage = reinterpret_cast<double*>(smem + STAGES * STAGE_BYTES + 256);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t bar0 = smem_addr(bars);
@@ -314,6 +316,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN + col_local), v);
                 tmem_wait_ld();
                 const int col0 = tn * BN + col_local;
+                // the chunk's column terms, loaded once (lane = column) into the warp's slot and read as broadcasts
+                double* cs = colstage + ew * COLSTAGE_DOUBLES;
+                if (col0 < n) {                  // warp-uniform (n % 32 == 0)
+                    __syncwarp();
+                    cs[lane] = cp.colscale[col0 + lane];
+                    cs[32 + lane] = cp.colg[col0 + lane];
+                    cs[64 + lane] = cp.sB[col0 + lane];
+                    __syncwarp();
+                }
                 if (rv && col0 < n) {            // n % 32 == 0: the 32 columns are all in range or all out
                     // every xmax >= min(thr / (2 F1), sqrt(thr / F2) / 2) (sqrt(F1^2 + 4 F2 thr) <= F1 + 2 sqrt(F2 thr)).
                     // With D = v derate 2^r_i 2^c_j, that bound is >= b = best (1 + 2^-8) exactly when
@@ -333,16 +344,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 32; e++) {   // fully unrolled: v[] stays in registers
                         const int col = col0 + e;
-                        const double cJ = cp.colscale[col];
+                        const double cJ = cs[e];
                         const double vd = (double)__uint_as_float(v[e]);
                         const double D = __dmul_rn(__dmul_rn(__dmul_rn(vd, cp.derate), rI), cJ);
                         if (cp.dbg_D) cp.dbg_D[(size_t)row * n + col] = D;
                         if (!(D > 0.0)) { unc++; continue; }
-                        const double gh = cp.colg[col] + hI;
+                        const double gh = cs[32 + e] + hI;
                         if (vd >= T2 && vd >= beta * gh && gh >= 0x1p-1000) continue;
                         const double tD = __dmul_rn(cp.tau, D);
                         const double thr = cp.safety_pow2 ? __dmul_rn(tD, cp.inv_safety) : __ddiv_rn(tD, cp.safety);
-                        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cp.sB[col]), __dmul_rn(cJ, sAi)));
+                        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cs[64 + e]), __dmul_rn(cJ, sAi)));
                         const double F2 = __dmul_rn(f2r, cJ);
                         const double disc = fma(F1, F1, 4.0 * F2 * thr);
                         const double L = 2.0 * thr * rcp_approx(F1 + disc * rsqrt_approx(disc)) * (1.0 - 0x1p-8);
