@@ -56,6 +56,7 @@ def parse():
                          "full-matrix certificate; config: the single-graph path with (N, p) given (the sampled "
                          "rule's choice); persist: PersistA, A encoded once per step and --q products")
     ap.add_argument("--q", type=int, default=4, help="products per step in --mode persist")
+    ap.add_argument("--planes", type=int, default=0, help="force the plane count N (0: the workload's rule)")
     return ap.parse_args()
 
 
@@ -273,6 +274,8 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     m, k, n, phi, alt, forceN, desc = pkg.CONFIGS[args.workload]
+    if args.planes:
+        forceN = args.planes
 
     # inputs: generated on the host (numpy, seed 0); rank a S + b of the R x S grid holds A's row block a and B's
     # column block b (R = world, S = 1 for a plain row split)
