@@ -170,6 +170,12 @@ int ozk_gemm_residues(const int8_t* Ares, const int8_t* Bres, int m, int n, int 
  * product of ozaki_engine.py:1336, exact while k <= 131071).                                                 */
 int ozk_gemm_i32(const int8_t* A_plane, const int8_t* B_plane, int m, int n, int k, int32_t* C32, int32_t* err,
                  ozk_stream_t stream);
+/* Self-test of the GEMM's failure path (the reference has none: its waits are cuBLASLt's and the host's).
+ * One CTA runs the GEMM's roles over mbarriers that nothing arrives on: role 0 (the TMA producer) or role 1
+ * (an epilogue warp) waits limit_ns (1 us .. 4 s) of wall time, gives up, ORs its OZK_DEVERR_TIMEOUT_* flag
+ * into *err and raises the CTA's abort flag; the other role leaves through that flag; the TMEM the CTA holds is
+ * freed and the kernel returns.  waited_ns: device int64[2], the wall time each role waited (producer first).    */
+int ozk_wait_selftest(int role, int64_t limit_ns, int32_t* err, int64_t* waited_ns, ozk_stream_t stream);
 
 /* ---- stage 3c: CRT reconstruction and unscale (replaces recon_k, ozaki_engine.py:1040-1101) ------------- *
  * C[i][j] = the correctly rounded double of the symmetric CRT lift of X[.][i][j], times 2^(r_i + c_j - 2p)

@@ -273,6 +273,51 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---- bounded-wait self-test ----------------------------------------------------------------------------------
+// gemm_tc_kernel's failure path in miniature, on one CTA: warp 0 (the producer's role) and warp 2 (an epilogue
+// role) each wait on an mbarrier that nothing arrives on, while warp 1 holds 32 TMEM columns as the GEMM's warp 1
+// holds the accumulators.  The role named by `role` (0 = producer, 1 = epilogue) waits with `limit_ns`; the other
+// waits with WAIT_LIMIT_NS and the abort flag, so it leaves through the flag that the timed-out role raises, not
+// through its own limit.  Each role records how long it waited; TMEM is freed after both have returned, as at the
+// end of gemm_tc_kernel.
+__global__ void __launch_bounds__(96, 1)
+    wait_selftest_kernel(int role, uint64_t limit_ns, int32_t* __restrict__ err, long long* __restrict__ waited_ns) {
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_addr(&bars[0]), 1);
+        mbar_init(smem_addr(&bars[1]), 1);
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(&tmem_slot), 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_slot;
+    if ((warp == 0 || warp == 2) && lane == 0) {
+        const int me = warp == 0 ? 0 : 1;
+        const uint64_t t0 = global_timer_ns();
+        // phase 0 of a fresh barrier completes only after one arrival, and none comes
+        const bool ok = mbar_wait_bounded(smem_addr(&bars[me]), 0u, &abort_flag, me == role ? limit_ns : WAIT_LIMIT_NS);
+        waited_ns[me] = (long long)(global_timer_ns() - t0);
+        if (!ok && !abort_flag)
+            raise_abort(&abort_flag, err, me == 0 ? OZK_DEVERR_TIMEOUT_PRODUCER : OZK_DEVERR_TIMEOUT_EPILOGUE);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, 32);
+    }
+}
+
 // ---- host side ------------------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -381,6 +426,19 @@ extern "C" int ozk_gemm_i32(const int8_t* A_plane, const int8_t* B_plane, int m,
                             int32_t* err, ozk_stream_t stream) {
     if (!shapes_ok(A_plane, B_plane, C32, err, m, n, k) || k > OZK_KSEG) return OZK_ERR_ARG;
     return launch_gemm<MODE_I32>(A_plane, B_plane, m, n, k, 1, C32, err, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ozk_wait_selftest(int role, int64_t limit_ns, int32_t* err, int64_t* waited_ns, ozk_stream_t stream) {
+    if (!err || !waited_ns || (reinterpret_cast<uintptr_t>(waited_ns) & 7) || role < 0 || role > 1 ||
+        limit_ns < 1000 || limit_ns > (int64_t)WAIT_LIMIT_NS)
+        return OZK_ERR_ARG;
+    DeviceInfo* d = nullptr;
+    const int rc = device_info(&d);
+    if (rc != OZK_OK) return rc;
+    wait_selftest_kernel<<<1, 96, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        role, (uint64_t)limit_ns, err, reinterpret_cast<long long*>(waited_ns));
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
 }
 
 extern "C" int ozk_device_sm_count(int* out) {

@@ -94,6 +94,11 @@ def test_capi_host_calls_without_device(pkg):
     assert lib.ozk_split_a(None, None, None, None, 4, 32, 16, None, None) == -1
     assert lib.ozk_gemm_residues(None, None, 4, 32, 32, 16, None, None, None) == -1
     assert lib.ozk_reconstruct(None, None, None, None, 4, 32, 16, None, None) == -1
+    assert lib.ozk_wait_selftest(0, 10**6, None, None, None) == -1
+    assert lib.ozk_wait_selftest(2, 10**6, 16, 16, None) == -1           # role outside {0, 1}
+    assert lib.ozk_wait_selftest(0, 999, 16, 16, None) == -1             # limit below 1 us
+    assert lib.ozk_wait_selftest(1, 5 * 10**9, 16, 16, None) == -1       # limit above the GEMM's 4 s
+    assert lib.ozk_wait_selftest(0, 10**6, 16, 20, None) == -1           # waited_ns not 8-byte aligned
     with pytest.raises(pkg._lib.OzkError):
         pkg._lib.check(-5, "probe")
 
