@@ -16,10 +16,9 @@
 // 128-byte swizzle, FP32 accumulators double-buffered in TMEM), whose 8 epilogue warps evaluate the bound for every
 // entry straight out of TMEM and reduce min xmax / the uncertified count per warp, so the m x n matrix D never
 // reaches HBM (an optional debug output writes D).  Only the minimum matters, so an entry is skipped once a lower
-// bound of its xmax cannot beat the running minimum (published across CTAs after every tile): first a
-// division-free test against per-tile thresholds, then the formula with approximate reciprocals, both with a 2^-8
-// margin; the exact reference formula runs only for the entries near the minimum.  Waits are bounded; no cluster
-// multicast.
+// bound of its xmax cannot beat the running minimum (published across CTAs after every tile): the formula with
+// approximate reciprocals and a 2^-8 margin, evaluated without branches for 32 entries at a time; the exact
+// reference formula runs only for the entries near the minimum.  Waits are bounded; no cluster multicast.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -41,7 +40,7 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
 constexpr uint32_t IDESC = umma_idesc_f16_f32(BM, BN);
 constexpr int NUM_BARS = 2 * STAGES + 5;
-constexpr int COLSTAGE_DOUBLES = 3 * 32;          // per epilogue warp: 2^c_j, g_j, sB_j of its 32 columns
+constexpr int COLSTAGE_DOUBLES = 2 * 32;          // per epilogue warp: 2^c_j, sB_j of its 32 columns
 constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256 + (size_t)EPI_WARPS * COLSTAGE_DOUBLES * 8;
 constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;
 constexpr unsigned long long kEmpty = 0xFFFFFFFFFFFFFFFFull;   // "no certified entry" (above every double's bits)
@@ -53,10 +52,9 @@ struct CertParams {
     const double* colscale;   // 2^c_j
     const double* sA;
     const double* sB;
-    const double* colg;                // sB_j / 2^c_j (the skip test's column term)
     double derate, tau, safety, f2k;   // 1 - 8 k 2^-24, tau, safety, 0.25 k
-    double kappa;                      // safety / (tau derate)
     double inv_safety;                 // 1 / safety when safety is a power of two (then x / safety == x * inv_safety)
+    double rcp_safety;                 // inv_safety, or RN(1 / safety) when safety is not a power of two
     int safety_pow2;
     int m, n, k;
     unsigned long long* xmin;          // bit pattern of min xmax over certified entries (atomicMin)
@@ -102,17 +100,13 @@ constexpr int kT = 64;
 __global__ void __launch_bounds__(256) cert_prep_b_kernel(const double* __restrict__ B, const double* __restrict__ g,
                                                           const double* __restrict__ ig, const int32_t* __restrict__ c,
                                                           int k, int n, __half* __restrict__ B16t,
-                                                          double* __restrict__ colscale, const double* __restrict__ sB,
-                                                          double* __restrict__ colg) {
+                                                          double* __restrict__ colscale) {
     __shared__ __half tile[kT][kT + 2];
     const int l0 = blockIdx.y * kT, j0 = blockIdx.x * kT;
     const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4
     const int j = j0 + tx;
     const double scj = j < n ? pow2i(-c[j]) : 0.0;
-    if (blockIdx.y == 0 && ty == 0 && j < n) {
-        colscale[j] = pow2i(c[j]);
-        colg[j] = sB[j] * scj;          // sB_j / 2^c_j (inf or NaN when 2^-c_j overflows: then nothing is skipped)
-    }
+    if (blockIdx.y == 0 && ty == 0 && j < n) colscale[j] = pow2i(c[j]);
     for (int yy = ty; yy < kT; yy += 4) {
         const int l = l0 + yy;
         __half h = __float2half_rn(0.0f);
@@ -303,7 +297,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool rv = row < m;
             const double rI = rv ? cp.rowscale[row] : 0.0, sAi = rv ? cp.sA[row] : 0.0;
             const double f2r = __dmul_rn(cp.f2k, rI);                // (0.25 k) 2^r_i
-            const double hI = rv ? __ddiv_rn(sAi, rI) : 0.0;           // sA_i / 2^r_i (the skip test's row term)
             // the smallest xmax found so far by any CTA: entries whose lower bound is above it are skipped
             {
                 const unsigned long long gb = *reinterpret_cast<volatile unsigned long long*>(cp.xmin);
@@ -321,46 +314,51 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (col0 < n) {                  // warp-uniform (n % 32 == 0)
                     __syncwarp();
                     cs[lane] = cp.colscale[col0 + lane];
-                    cs[32 + lane] = cp.colg[col0 + lane];
-                    cs[64 + lane] = cp.sB[col0 + lane];
+                    cs[32 + lane] = cp.sB[col0 + lane];
                     __syncwarp();
                 }
                 if (rv && col0 < n) {            // n % 32 == 0: the 32 columns are all in range or all out
-                    // every xmax >= min(thr / (2 F1), sqrt(thr / F2) / 2) (sqrt(F1^2 + 4 F2 thr) <= F1 + 2 sqrt(F2 thr)).
-                    // With D = v derate 2^r_i 2^c_j, that bound is >= b = best (1 + 2^-8) exactly when
-                    //   v >= beta (g_j + h_i),  beta = b safety / (tau derate), g_j = sB_j / 2^c_j, h_i = sA_i / 2^r_i,
-                    //   v >= T2 = b^2 k safety / (tau derate);
-                    // the 2^-8 margin is far above the rounding of these and of the reference formula, so such an
-                    // entry cannot be below the current minimum and is skipped.  No skipping while the thresholds
-                    // could underflow (b < 2^-400, g_j + h_i < 2^-1000) or when they overflow or are NaN.  That bound
-                    // can be 2x below xmax; an entry it keeps is then tested with the formula itself, evaluated with
-                    // the approximate reciprocal and reciprocal square root and lowered by 2^-8, and only an entry
-                    // within that margin of the minimum (or one whose estimate is not finite) is evaluated exactly.
+                    // Pass 1, branch-free over the chunk (the 32 entries' dependency chains interleave): a lower
+                    // bound L of each entry's xmax, the reference formula evaluated with the approximate reciprocal
+                    // and reciprocal square root and lowered by 2^-8.  An entry with L >= the current minimum cannot
+                    // lower it and is skipped; the margin is far above the error of the approximations and of
+                    // thr1 (tau D) * (1 / safety), which is thr itself when safety is a power of two and otherwise
+                    // within an ulp of it, unless it is below 2^-1000, where no entry is skipped.  Entries with
+                    // D <= 0 (or NaN) are uncertified.  Pass 2 evaluates the kept entries exactly, in the
+                    // reference's operation order; near the end of a run it is rarely taken.
                     const double bestd = best == kEmpty ? INFINITY : __longlong_as_double((long long)best);
-                    const double bm = bestd * (1.0 + 0x1p-8);
-                    const bool can_skip = bm >= 0x1p-400 && cp.kappa > 0.0 && cp.kappa < INFINITY;
-                    const double beta = can_skip ? bm * cp.kappa : INFINITY;
-                    const double T2 = can_skip ? bm * bm * (double)cp.k * cp.kappa : INFINITY;
+                    uint32_t keep = 0;
 #pragma unroll
                     for (int e = 0; e < 32; e++) {   // fully unrolled: v[] stays in registers
-                        const int col = col0 + e;
                         const double cJ = cs[e];
                         const double vd = (double)__uint_as_float(v[e]);
                         const double D = __dmul_rn(__dmul_rn(__dmul_rn(vd, cp.derate), rI), cJ);
-                        if (cp.dbg_D) cp.dbg_D[(size_t)row * n + col] = D;
-                        if (!(D > 0.0)) { unc++; continue; }
-                        const double gh = cs[32 + e] + hI;
-                        if (vd >= T2 && vd >= beta * gh && gh >= 0x1p-1000) continue;
-                        const double tD = __dmul_rn(cp.tau, D);
-                        const double thr = cp.safety_pow2 ? __dmul_rn(tD, cp.inv_safety) : __ddiv_rn(tD, cp.safety);
-                        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cs[64 + e]), __dmul_rn(cJ, sAi)));
+                        if (cp.dbg_D) cp.dbg_D[(size_t)row * n + col0 + e] = D;
+                        const bool pos = D > 0.0;
+                        unc += pos ? 0ull : 1ull;
+                        const double thr1 = __dmul_rn(__dmul_rn(cp.tau, D), cp.rcp_safety);
+                        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cs[32 + e]), __dmul_rn(cJ, sAi)));
                         const double F2 = __dmul_rn(f2r, cJ);
-                        const double disc = fma(F1, F1, 4.0 * F2 * thr);
-                        const double L = 2.0 * thr * rcp_approx(F1 + disc * rsqrt_approx(disc)) * (1.0 - 0x1p-8);
-                        if (L >= bestd && L < INFINITY) continue;
-                        const double x = entry_xmax(thr, F1, F2);
-                        const unsigned long long xb = (unsigned long long)__double_as_longlong(x);
-                        if (!(x != x) && xb < best) best = xb;           // NaN bounds are not minima
+                        const double disc = fma(F1, F1, 4.0 * F2 * thr1);
+                        const double L = 2.0 * thr1 * rcp_approx(F1 + disc * rsqrt_approx(disc)) * (1.0 - 0x1p-8);
+                        const bool skip = L >= bestd && L < INFINITY && (cp.safety_pow2 || thr1 >= 0x1p-1000);
+                        keep |= (pos && !skip) ? (1u << e) : 0u;
+                    }
+                    if (keep) {
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            if (!(keep & (1u << e))) continue;
+                            const double cJ = cs[e];
+                            const double vd = (double)__uint_as_float(v[e]);
+                            const double D = __dmul_rn(__dmul_rn(__dmul_rn(vd, cp.derate), rI), cJ);
+                            const double tD = __dmul_rn(cp.tau, D);
+                            const double thr = cp.safety_pow2 ? __dmul_rn(tD, cp.inv_safety) : __ddiv_rn(tD, cp.safety);
+                            const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cs[32 + e]), __dmul_rn(cJ, sAi)));
+                            const double F2 = __dmul_rn(f2r, cJ);
+                            const double x = entry_xmax(thr, F1, F2);
+                            const unsigned long long xb = (unsigned long long)__double_as_longlong(x);
+                            if (!(x != x) && xb < best) best = xb;           // NaN bounds are not minima
+                        }
                     }
                 }
             }
@@ -430,7 +428,7 @@ bool g_attr[64];
 extern "C" size_t ozk_certificate_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
     return align256((size_t)m * k * 2) + align256((size_t)n * k * 2) + align256((size_t)m * 8) +
-           2 * align256((size_t)n * 8) + 2 * align256((size_t)k * 8) + 256;
+           align256((size_t)n * 8) + 2 * align256((size_t)k * 8) + 256;
 }
 
 extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, int k, const int32_t* gam,
@@ -464,7 +462,6 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     double* colscale = rowscale + align256((size_t)m * 8) / 8;
     double* g = colscale + align256((size_t)n * 8) / 8;
     double* ig = g + align256((size_t)k * 8) / 8;
-    double* colg = ig + align256((size_t)k * 8) / 8;
 
     if (cudaMemsetAsync(xmin, 0xFF, 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
     if (cudaMemsetAsync(uncertified, 0, 8, st) != cudaSuccess) return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
@@ -473,8 +470,7 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     OZK_CHECK_LAUNCH();
     cert_prep_a_kernel<<<dim3(bx, m < 65535 ? m : 65535), 256, 0, st>>>(A, g, r, m, k, reinterpret_cast<__half2*>(A16), rowscale);
     OZK_CHECK_LAUNCH();
-    cert_prep_b_kernel<<<dim3((n + kT - 1) / kT, (k + kT - 1) / kT), 256, 0, st>>>(B, g, ig, c, k, n, B16t, colscale, sB,
-                                                                                       colg);
+    cert_prep_b_kernel<<<dim3((n + kT - 1) / kT, (k + kT - 1) / kT), 256, 0, st>>>(B, g, ig, c, k, n, B16t, colscale);
     OZK_CHECK_LAUNCH();
 
     CUtensorMap ta, tb;
@@ -486,7 +482,6 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
     cp.colscale = colscale;
     cp.sA = sA;
     cp.sB = sB;
-    cp.colg = colg;
     cp.derate = 1.0 - 8.0 * (double)k * 0x1p-24;
     cp.tau = tau;
     cp.safety = safety;
@@ -495,9 +490,9 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
         const double fr = frexp(safety, &e2);
         cp.safety_pow2 = (fr == 0.5) ? 1 : 0;                  // safety = 2^(e2 - 1)
         cp.inv_safety = cp.safety_pow2 ? ldexp(1.0, 1 - e2) : 0.0;
+        cp.rcp_safety = cp.safety_pow2 ? cp.inv_safety : 1.0 / safety;
     }
     cp.f2k = 0.25 * (double)k;
-    cp.kappa = safety / (tau * cp.derate);
     cp.m = m;
     cp.n = n;
     cp.k = k;

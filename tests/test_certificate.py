@@ -31,6 +31,45 @@ def _tol(k):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("m,k,n,phi,safety", [(4096, 64, 4096, 0.5, 2.0), (2048, 96, 1024, 2.0, 3.0),
+                                              (260, 544, 96, 1.0, 3.0), (128, 32, 256, 3.0, 0.75)])
+def test_certificate_min_is_exact_over_its_own_D(pkg, engine, m, k, n, phi, safety):
+    """The kernel skips entries whose xmax provably cannot lower the running minimum.  Its minimum must equal, bit for
+    bit, the minimum of the reference formula (:1565-1569) evaluated exactly over the kernel's own D (written out
+    through D_out), in the reference's operation order; the uncertified count is the number of entries with D <= 0.
+    4096 x 4096 gives 512 tiles, several per CTA, so the minimum published between tiles is exercised; safety 3 and
+    0.75 are not powers of two."""
+    import torch
+    from matrix_numbers_b200.certificate import certificate_device
+    tau = 2.0 ** -52
+    A, B = pkg.make_inputs(m, k, n, phi, seed=3 * m + n)
+    A[1, :] = 0.0
+    B[:, 2] = 0.0
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    b = _dev_stats(torch, engine, Ad, Bd)
+    Dd = torch.empty(m, n, dtype=torch.float64, device="cuda")
+    w = certificate_device(engine, Ad, Bd, b["gam"], b["r"], b["c"], b["sA"], b["sB"], tau=tau, safety=safety, D_out=Dd)
+    torch.cuda.synchronize()
+    assert int(w["err"].item()) == 0
+    D = Dd.cpu().numpy()
+    rI = np.ldexp(1.0, b["r"].cpu().numpy().astype(np.int64))[:, None]
+    cJ = np.ldexp(1.0, b["c"].cpu().numpy().astype(np.int64))[None, :]
+    sA = b["sA"].cpu().numpy()[:, None]
+    sB = b["sB"].cpu().numpy()[None, :]
+    with np.errstate(all="ignore"):
+        thr = (tau * D) / safety
+        F1 = 0.5 * (rI * sB + cJ * sA)
+        F2 = ((0.25 * k) * rI) * cJ
+        x = (2.0 * thr) / (F1 + np.sqrt(F1 * F1 + (4.0 * F2) * thr))
+    pos = D > 0
+    assert int(w["unc"].item()) == int((~pos).sum()) >= n + m - 1
+    cand = x[pos & ~np.isnan(x)].view(np.uint64)
+    want = int(cand.min()) if cand.size else 2 ** 64 - 1
+    got = int(w["xmin"].view(torch.int64).item()) & (2 ** 64 - 1)
+    assert got == want, (got, want)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("m,k,n,phi", [(128, 256, 256, 1.0), (260, 544, 96, 2.0), (512, 2048, 384, 0.5),
                                        (64, 96, 512, 3.0)])
 def test_certificate_kernel_vs_oracle(pkg, oracle, engine, m, k, n, phi):
