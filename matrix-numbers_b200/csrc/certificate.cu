@@ -16,9 +16,10 @@
 // 128-byte swizzle, FP32 accumulators double-buffered in TMEM), whose 8 epilogue warps evaluate the bound for every
 // entry straight out of TMEM and reduce min xmax / the uncertified count per warp, so the m x n matrix D never
 // reaches HBM (an optional debug output writes D).  Only the minimum matters, so an entry is skipped once a lower
-// bound of its xmax cannot beat the running minimum (published across CTAs after every tile): the formula with
-// approximate reciprocals and a 2^-8 margin, evaluated without branches for 32 entries at a time; the exact
-// reference formula runs only for the entries near the minimum.  Waits are bounded; no cluster multicast.
+// bound of its xmax cannot beat the running minimum (published across CTAs after every tile): a lower bound of the
+// formula in which the row and column scalings cancel, evaluated in FP32 without branches for 32 entries at a time
+// (fast_term); the exact reference formula runs only for the entries near the minimum and for rows or columns
+// outside that bound's range.  Waits are bounded; no cluster multicast.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -40,7 +41,7 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
 constexpr uint32_t IDESC = umma_idesc_f16_f32(BM, BN);
 constexpr int NUM_BARS = 2 * STAGES + 5;
-constexpr int COLSTAGE_DOUBLES = 2 * 32;          // per epilogue warp: 2^c_j, sB_j of its 32 columns
+constexpr int COLSTAGE_DOUBLES = 2 * 32 + 16;     // per epilogue warp: 2^c_j, sB_j (f64) and sB_j / 2^c_j (f32)
 constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256 + (size_t)EPI_WARPS * COLSTAGE_DOUBLES * 8;
 constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;
 constexpr unsigned long long kEmpty = 0xFFFFFFFFFFFFFFFFull;   // "no certified entry" (above every double's bits)
@@ -54,8 +55,8 @@ struct CertParams {
     const double* sB;
     double derate, tau, safety, f2k;   // 1 - 8 k 2^-24, tau, safety, 0.25 k
     double inv_safety;                 // 1 / safety when safety is a power of two (then x / safety == x * inv_safety)
-    double rcp_safety;                 // inv_safety, or RN(1 / safety) when safety is not a power of two
     int safety_pow2;
+    float c8, k4;                      // the fast bound's constants (fast_term); c8 NaN: no fast bound
     int m, n, k;
     unsigned long long* xmin;          // bit pattern of min xmax over certified entries (atomicMin)
     unsigned long long* uncertified;
@@ -141,15 +142,27 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int32_t* e
 }
 
 // fast approximations (hardware reciprocal / reciprocal square root, errors far below 2^-8), used only to skip entries
-__device__ __forceinline__ double rcp_approx(double x) {
-    double r;
-    asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(x));
+__device__ __forceinline__ float rcp_approx_f32(float x) {   // at most 1 ulp from 1 / x
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
-__device__ __forceinline__ double rsqrt_approx(double x) {
-    double r;
-    asm("rsqrt.approx.f64 %0, %1;" : "=d"(r) : "d"(x));
-    return r;
+
+// The fast lower bound.  With R = 2^r_i 2^c_j, D = v derate R, thr = kap v R (kap = tau derate / safety),
+// F1 = 0.5 R s and F2 = 0.25 k R, where s = sA_i / 2^r_i + sB_j / 2^c_j, the scalings cancel from the formula:
+//   xmax = 4 kap v / (s + sqrt(s^2 + 4 k kap v)),
+// and sqrt(s^2 + t) <= s + t / (2 s) gives  xmax >= 8 kap v s / (4 s^2 + 4 k kap v).
+// Evaluated in FP32 with c8 = 8 kap (1 - 2^-8) and k4 = 4 k kap, its error is a few 2^-23, far inside the 2^-8
+// margin, provided the reference's FP64 chain stays in the normal range, where it is within a few 2^-53 of the
+// exact formula.  That holds when 2^r_i and 2^c_j lie in [2^-200, 2^200], the row and column terms in
+// [2^-59, 2^60], v in {0} U [2^-48, 2^31] (sums of FP16 products of magnitudes below 1, k < 2^31) and tau and
+// safety in [2^-100, 2^100]; outside, fast_term returns NaN (or the host sets c8 to NaN) and every entry of that
+// row or column goes to the exact evaluation.  Inside, v = 0 gives D = 0 (uncertified); an entry with v > 0 is
+// either skipped by the bound or classified by the exact evaluation.
+__device__ __forceinline__ float fast_term(double s, double scale) {
+    const bool ok = scale >= 0x1p-200 && scale <= 0x1p200;
+    const double t = ok ? s / scale : 0.0;                       // exact scaling by a power of two
+    return (ok && t >= 0x1p-59 && t <= 0x1p60) ? __double2float_rn(t) : __int_as_float(0x7fffffff);
 }
 
 // xmax of one entry, in the reference's operation order: thr = (tau D) / safety, F1 = 0.5 (rI sB + cJ sA),
@@ -297,6 +310,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool rv = row < m;
             const double rI = rv ? cp.rowscale[row] : 0.0, sAi = rv ? cp.sA[row] : 0.0;
             const double f2r = __dmul_rn(cp.f2k, rI);                // (0.25 k) 2^r_i
+            const float aI = fast_term(sAi, rI);                       // sA_i / 2^r_i, or NaN: no fast bound
             // the smallest xmax found so far by any CTA: entries whose lower bound is above it are skipped
             {
                 const unsigned long long gb = *reinterpret_cast<volatile unsigned long long*>(cp.xmin);
@@ -311,39 +325,44 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int col0 = tn * BN + col_local;
                 // the chunk's column terms, loaded once (lane = column) into the warp's slot and read as broadcasts
                 double* cs = colstage + ew * COLSTAGE_DOUBLES;
+                float* bs = reinterpret_cast<float*>(cs + 64);
                 if (col0 < n) {                  // warp-uniform (n % 32 == 0)
                     __syncwarp();
-                    cs[lane] = cp.colscale[col0 + lane];
-                    cs[32 + lane] = cp.sB[col0 + lane];
+                    const double cj = cp.colscale[col0 + lane], sbj = cp.sB[col0 + lane];
+                    cs[lane] = cj;
+                    cs[32 + lane] = sbj;
+                    bs[lane] = fast_term(sbj, cj);                       // sB_j / 2^c_j, or NaN
                     __syncwarp();
                 }
                 if (rv && col0 < n) {            // n % 32 == 0: the 32 columns are all in range or all out
-                    // Pass 1, branch-free over the chunk (the 32 entries' dependency chains interleave): a lower
-                    // bound L of each entry's xmax, the reference formula evaluated with the approximate reciprocal
-                    // and reciprocal square root and lowered by 2^-8.  An entry with L >= the current minimum cannot
-                    // lower it and is skipped; the margin is far above the error of the approximations and of
-                    // thr1 (tau D) * (1 / safety), which is thr itself when safety is a power of two and otherwise
-                    // within an ulp of it, unless it is below 2^-1000, where no entry is skipped.  Entries with
-                    // D <= 0 (or NaN) are uncertified.  Pass 2 evaluates the kept entries exactly, in the
-                    // reference's operation order; near the end of a run it is rarely taken.
+                    // Pass 1, branch-free over the chunk (the 32 entries' dependency chains interleave), in FP32:
+                    // L = c8 v s / (4 s^2 + k4 v) <= xmax (1 - 2^-8) (see fast_term).  An entry with L >= the
+                    // current minimum (rounded up to FP32) cannot lower it and is skipped; an entry of a row and
+                    // column inside the fast bound's range with v = 0 has D = 0 and is uncertified.  Pass 2
+                    // evaluates every other entry exactly, in the reference's operation order; after the first
+                    // tiles of a run it is rarely taken.
                     const double bestd = best == kEmpty ? INFINITY : __longlong_as_double((long long)best);
-                    uint32_t keep = 0;
+                    const float best_up = __double2float_ru(bestd);
+                    if (cp.dbg_D) {                  // optional debug output of D
+#pragma unroll
+                        for (int e = 0; e < 32; e++)
+                            cp.dbg_D[(size_t)row * n + col0 + e] =
+                                __dmul_rn(__dmul_rn(__dmul_rn((double)__uint_as_float(v[e]), cp.derate), rI), cs[e]);
+                    }
+                    uint32_t keep = 0, zero = 0;
 #pragma unroll
                     for (int e = 0; e < 32; e++) {   // fully unrolled: v[] stays in registers
-                        const double cJ = cs[e];
-                        const double vd = (double)__uint_as_float(v[e]);
-                        const double D = __dmul_rn(__dmul_rn(__dmul_rn(vd, cp.derate), rI), cJ);
-                        if (cp.dbg_D) cp.dbg_D[(size_t)row * n + col0 + e] = D;
-                        const bool pos = D > 0.0;
-                        unc += pos ? 0ull : 1ull;
-                        const double thr1 = __dmul_rn(__dmul_rn(cp.tau, D), cp.rcp_safety);
-                        const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cs[32 + e]), __dmul_rn(cJ, sAi)));
-                        const double F2 = __dmul_rn(f2r, cJ);
-                        const double disc = fma(F1, F1, 4.0 * F2 * thr1);
-                        const double L = 2.0 * thr1 * rcp_approx(F1 + disc * rsqrt_approx(disc)) * (1.0 - 0x1p-8);
-                        const bool skip = L >= bestd && L < INFINITY && (cp.safety_pow2 || thr1 >= 0x1p-1000);
-                        keep |= (pos && !skip) ? (1u << e) : 0u;
+                        const float vf = __uint_as_float(v[e]);
+                        const float sf = aI + bs[e];
+                        const float den = __fmaf_rn(__fmul_rn(sf, sf), 4.0f, __fmul_rn(cp.k4, vf));
+                        const float L = __fmul_rn(__fmul_rn(__fmul_rn(vf, sf), rcp_approx_f32(den)), cp.c8);
+                        const bool in_range = sf == sf;
+                        const bool pos = vf > 0.0f;
+                        const bool above = L >= best_up && L >= 0x1p-100f && L < INFINITY;
+                        zero |= (in_range && !pos) ? (1u << e) : 0u;
+                        keep |= (in_range && (!pos || above)) ? 0u : (1u << e);
                     }
+                    unc += (unsigned long long)__popc(zero);
                     if (keep) {
 #pragma unroll
                         for (int e = 0; e < 32; e++) {
@@ -351,6 +370,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             const double cJ = cs[e];
                             const double vd = (double)__uint_as_float(v[e]);
                             const double D = __dmul_rn(__dmul_rn(__dmul_rn(vd, cp.derate), rI), cJ);
+                            if (!(D > 0.0)) { unc++; continue; }                  // uncertified
                             const double tD = __dmul_rn(cp.tau, D);
                             const double thr = cp.safety_pow2 ? __dmul_rn(tD, cp.inv_safety) : __ddiv_rn(tD, cp.safety);
                             const double F1 = __dmul_rn(0.5, __dadd_rn(__dmul_rn(rI, cs[32 + e]), __dmul_rn(cJ, sAi)));
@@ -490,9 +510,16 @@ extern "C" int ozk_certificate(const double* A, const double* B, int m, int n, i
         const double fr = frexp(safety, &e2);
         cp.safety_pow2 = (fr == 0.5) ? 1 : 0;                  // safety = 2^(e2 - 1)
         cp.inv_safety = cp.safety_pow2 ? ldexp(1.0, 1 - e2) : 0.0;
-        cp.rcp_safety = cp.safety_pow2 ? cp.inv_safety : 1.0 / safety;
     }
     cp.f2k = 0.25 * (double)k;
+    {
+        const double kap = tau * cp.derate / safety;
+        const double c8 = 8.0 * kap * (1.0 - 0x1p-8), k4 = 4.0 * (double)k * kap;
+        const bool ok = tau >= 0x1p-100 && tau <= 0x1p100 && safety >= 0x1p-100 && safety <= 0x1p100 &&
+                        c8 >= 0x1p-110 && c8 <= 0x1p110 && k4 >= 0x1p-110 && k4 <= 0x1p110;
+        cp.c8 = ok ? (float)c8 : nanf("");
+        cp.k4 = ok ? (float)k4 : 0.0f;
+    }
     cp.m = m;
     cp.n = n;
     cp.k = k;
