@@ -19,6 +19,53 @@ def test_oracle_certificate_is_a_lower_bound(pkg, oracle):
     assert np.all(cert["D"][:, 3] == 0)
 
 
+def test_fast_bound_is_below_the_formula():
+    """The certificate kernel skips an entry when an FP32 lower bound of its xmax is at or above the running minimum
+    (csrc/certificate.cu, fast_term): with the row and column scalings cancelled, L = c8 v s / (4 s^2 + k4 v).
+    Over the whole range where the kernel uses it (2^r, 2^c in [2^-200, 2^200], row and column terms in
+    [2^-59, 2^60], v in [2^-48, 2^31], tau and safety in [2^-100, 2^100]) L must stay below the reference's FP64
+    chain, with the reciprocal one ulp high (the worst case of rcp.approx.f32), and within 2^-7 of it on ordinary
+    data (so that it does skip)."""
+    rng = np.random.default_rng(1)
+    f32 = np.float32
+    checked = 0
+    for trial in range(120):
+        n = 4000
+        ext = trial % 4
+        r = rng.integers(-200, 201, n) if ext else rng.integers(-5, 6, n)
+        c = rng.integers(-200, 201, n) if ext else rng.integers(-5, 6, n)
+        a = np.exp2(rng.uniform(-59, 60, n)) if ext == 1 else np.exp2(rng.uniform(-1, 12, n))
+        b = np.exp2(rng.uniform(-59, 60, n)) if ext == 2 else np.exp2(rng.uniform(-1, 12, n))
+        v32 = (np.exp2(rng.uniform(-48, 31, n)) if ext == 3 else rng.uniform(1, 4096, n)).astype(f32)
+        v = v32.astype(np.float64)
+        k = int(rng.choice([32, 4096, 65536, 262144]))
+        tau = 2.0 ** rng.uniform(-100, 100) if ext else 2.0 ** -52
+        safety = 2.0 ** rng.uniform(-100, 100) if ext else float(rng.choice([2.0, 3.0, 0.75]))
+        derate = 1.0 - 8.0 * k * 2.0 ** -24
+        kap = tau * derate / safety
+        c8, k4 = 8.0 * kap * (1 - 2.0 ** -8), 4.0 * k * kap
+        if not (2.0 ** -110 <= c8 <= 2.0 ** 110 and 2.0 ** -110 <= k4 <= 2.0 ** 110):
+            continue                                          # the kernel's host code disables the bound there
+        rI, cJ = np.ldexp(1.0, r), np.ldexp(1.0, c)
+        sA, sB = a * rI, b * cJ
+        with np.errstate(all="ignore"):
+            D = ((v * derate) * rI) * cJ
+            thr = (tau * D) / safety
+            F1 = 0.5 * (rI * sB + cJ * sA)
+            F2 = ((0.25 * k) * rI) * cJ
+            x = (2.0 * thr) / (F1 + np.sqrt(F1 * F1 + (4.0 * F2) * thr))
+            s = (sA / rI).astype(f32) + (sB / cJ).astype(f32)
+            den = (s * s) * f32(4.0) + f32(k4) * v32
+            L = ((v32 * s) * np.nextafter(f32(1.0) / den, f32(np.inf))) * f32(c8)
+        used = (L >= 2.0 ** -100) & np.isfinite(L)
+        ratio = L[used].astype(np.float64) / x[used]
+        assert ratio.max() < 1.0
+        if ext == 0:
+            assert ratio.min() > 1.0 - 2.0 ** -7
+        checked += int(used.sum())
+    assert checked > 200000
+
+
 def _dev_stats(torch, E, Ad, Bd):
     m, k = Ad.shape
     b = E.buffers(m, Bd.shape[1], k, 20)
