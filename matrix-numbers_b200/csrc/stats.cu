@@ -114,18 +114,45 @@ __device__ __forceinline__ double scale2(double x, int e) {
 //   s = sum |x| 2^g,  q = sum (|x| 2^(g - emax))^2.
 // When emax grows by d, q is rescaled by 2^-2d (an exact power-of-two scaling), so one pass gives the same sums as the
 // reference's two passes (max first, then sums relative to it) up to the order of additions.
+//
+// add_abs is the per-element entry: z = |x| 2^g is formed by one multiplication with a power of two built from its
+// bits, which is exact while z is normal; then e(z) = e(x) + g is read from z's exponent field, s += z, and
+// y = z 2^-emax uses R = 2^-emax kept in a register.  Each of s, y and q is the same correctly rounded value as in the
+// general path (add), so the results are bitwise the same; elements whose z is not normal or whose running maximum
+// leaves [-1022, 1022] take the general path.
 struct RunStats {
     int emax;
-    double s, q;
-    __device__ __forceinline__ void init() { emax = OZK_NEG; s = 0.0; q = 0.0; }
+    double s, q, R;                 // R = 2^-emax while emax is in [-1022, 1022], else 0
+    __device__ __forceinline__ void init() { emax = OZK_NEG; s = 0.0; q = 0.0; R = 0.0; }
+    __device__ __forceinline__ void set_emax(int e) {
+        emax = e;
+        R = (e >= -1022 && e <= 1022) ? __hiloint2double((1023 - e) << 20, 0) : 0.0;
+    }
     __device__ __forceinline__ void add(double x, int e_plus_g, int g) {   // x = |value| != 0
         if (e_plus_g > emax) {
             if (emax != OZK_NEG) q = scale2(q, -2 * (e_plus_g - emax));
-            emax = e_plus_g;
+            set_emax(e_plus_g);
         }
         s += scale2(x, g);
         const double y = scale2(x, g - emax);
         q = fma(y, y, q);
+    }
+    __device__ __forceinline__ void add_abs(double a, int g) {            // a = |value|, zero allowed
+        const bool gok = g >= -1022 && g <= 1023;
+        const double z = a * __hiloint2double((gok ? g + 1023 : 1023) << 20, 0);
+        const int ez = (int)((unsigned)__double2hiint(z) >> 20);           // biased exponent (z >= 0)
+        const int e = ez - 1022;                                            // frexp exponent of z
+        if (gok && ez >= 1 && ez <= 2046 && (e > emax ? e <= 1022 : R != 0.0)) {
+            if (e > emax) {
+                if (emax != OZK_NEG) q = scale2(q, -2 * (e - emax));
+                set_emax(e);
+            }
+            s += z;
+            const double y = z * R;
+            q = fma(y, y, q);
+        } else if (a != 0.0) {
+            add(a, ozk_fexp(ozk_bits(a)) + g, g);
+        }
     }
 };
 
@@ -144,9 +171,8 @@ __global__ void __launch_bounds__(kThreads) rowstats_a_kernel(const double* __re
     for (int h = threadIdx.x; h < k / 2; h += kThreads) {
         const double2 v = __ldg(row + h);
         const int2 g = __ldg(g2 + h);
-        const int e0 = ozk_fexp(ozk_bits(v.x) & OZK_ABSMASK), e1 = ozk_fexp(ozk_bits(v.y) & OZK_ABSMASK);
-        if (e0 != OZK_NEG) rs.add(fabs(v.x), e0 + g.x, g.x);
-        if (e1 != OZK_NEG) rs.add(fabs(v.y), e1 + g.y, g.y);
+        rs.add_abs(fabs(v.x), g.x);
+        rs.add_abs(fabs(v.y), g.y);
     }
     const int mx = block_reduce(rs.emax, (int)OZK_NEG, smi, MaxI());
     const int rr = mx <= OZK_NEG / 2 ? 0 : mx;
@@ -170,9 +196,8 @@ __global__ void __launch_bounds__(kThreads) colstats_b_kernel(const double* __re
     for (int l = l0; l < l1; l++) {
         const double2 v = __ldg(reinterpret_cast<const double2*>(B + (size_t)l * n + j));
         const int g = -__ldg(gam + l);
-        const int e0 = ozk_fexp(ozk_bits(v.x) & OZK_ABSMASK), e1 = ozk_fexp(ozk_bits(v.y) & OZK_ABSMASK);
-        if (e0 != OZK_NEG) r0.add(fabs(v.x), e0 + g, g);
-        if (e1 != OZK_NEG) r1.add(fabs(v.y), e1 + g, g);
+        r0.add_abs(fabs(v.x), g);
+        r1.add_abs(fabs(v.y), g);
     }
     const size_t o = (size_t)blockIdx.y * n + j;
     pc[o] = r0.emax; pc[o + 1] = r1.emax;

@@ -87,6 +87,34 @@ def test_stats_random(pkg, oracle, torch_mod, shape, phi, inside):
     assert_stats_equal(got, oracle.stats(A, B, inside))
 
 
+def test_stats_extreme_exponents(pkg, oracle, torch_mod):
+    """Entries across the whole double range: subnormal rows and columns, 2^-1070 next to 2^1014 in one row, zeros.
+    The scaled values |x| 2^gamma then leave the normal range, so the statistics' general path runs beside the fast
+    one (csrc/stats.cu, RunStats.add_abs); both must agree with the oracle, with inside scaling on and off."""
+    torch = torch_mod
+    rng = np.random.default_rng(7)
+    m, k, n = 64, 256, 96
+
+    def mat(r, c):
+        x = rng.uniform(1.0, 2.0, (r, c)) * np.ldexp(1.0, rng.integers(-1070, 1015, (r, c)))
+        x *= rng.choice([-1.0, 1.0], (r, c))
+        x[rng.random((r, c)) < 0.1] = 0.0
+        return x
+
+    A, B = mat(m, k), mat(k, n)
+    A[0] = np.ldexp(rng.uniform(1.0, 2.0, k), rng.integers(-1074, -1023, k))     # subnormal row
+    A[1] = np.ldexp(rng.uniform(1.0, 2.0, k), rng.integers(990, 1020, k))        # huge row
+    A[2] = 0.0
+    B[:, 0] = np.ldexp(rng.uniform(1.0, 2.0, k), rng.integers(-1074, -1023, k))  # subnormal column
+    B[:, 1] = -np.ldexp(rng.uniform(1.0, 2.0, k), rng.integers(990, 1020, k))    # huge column
+    A[:, 3] = np.ldexp(rng.uniform(1.0, 2.0, m), rng.integers(-1074, -1060, m))  # gamma_3 above 1023
+    B[3, :] = np.ldexp(rng.uniform(1.0, 2.0, n), rng.integers(1005, 1015, n))
+    assert np.all(np.isfinite(A)) and np.all(np.isfinite(B))
+    for inside in (True, False):
+        got = host(dev_stats(pkg, torch, T(torch, A), T(torch, B), inside))
+        assert_stats_equal(got, oracle.stats(A, B, inside))
+
+
 def test_stats_nonfinite_flag(pkg, torch_mod):
     torch = torch_mod
     A, B = pkg.make_inputs(64, 64, 64, 1.0, seed=1)
