@@ -35,9 +35,11 @@ sys.path.insert(0, ROOT)
 import __graft_entry__  # noqa: E402
 
 METRIC = "emulated FP64 GEMM TFLOPS (2MNK/t) at n=16384, 1-8 B200; max rel error"
-# DRAM bytes (read + write) of one gemm_tc_kernel launch on one GPU, from one-pass ncu captures of this bench's own
-# command (profiles/dram_traffic_c3_n16384.md); workloads without a capture report null
+# DRAM bytes (read + write) of one gemm_tc_kernel launch on one GPU: constants from one-pass ncu captures
+# (dram__bytes_read.sum + dram__bytes_write.sum) of this bench's own command at the named workload; other workloads
+# report null.  They are not measured by the bench run itself ("traffic_source" in the JSON line says so).
 GEMM_TRAFFIC_BYTES = {"c3": 66.9e9 + 4.8e9, "c2": 537.7e6 + 242.9e6}
+GEMM_TRAFFIC_SOURCE = "constant from a one-pass ncu capture of `bench.py --workload {w}` (not measured in this run)"
 
 
 def parse():
@@ -57,7 +59,22 @@ def parse():
                          "rule's choice); persist: PersistA, A encoded once per step and --q products")
     ap.add_argument("--q", type=int, default=4, help="products per step in --mode persist")
     ap.add_argument("--planes", type=int, default=0, help="force the plane count N (0: the workload's rule)")
+    ap.add_argument("--clock-log", default="", help="also write the raw nvidia-smi clock samples to this CSV file")
     return ap.parse_args()
+
+
+def workload_config(args, m, n, k, phi, planes, p, world, grid, products=1):
+    """The `config` object of the JSON line, the same for both arms (the reference arm adds only its sample)."""
+    R, S = grid
+    return {"workload": args.workload, "desc": _desc(args.workload), "m": m, "n": n, "k": k, "phi": phi,
+            "planes": planes, "p": p, "mode": args.mode, "products_per_step": products,
+            "parallelism": f"{R} x {S} grid of C blocks" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (2 x 2.1 GB fp64)"}
+
+
+def _desc(workload):
+    pkg = __graft_entry__.load_package()
+    return pkg.CONFIGS[workload][6]
 
 
 # ------------------------------------------------------------------------------------------------ clocks
@@ -150,23 +167,49 @@ def int8_peak_tops(torch, dev):
 
 
 # ------------------------------------------------------------------------------------------------ CPU baseline
-def cpu_baseline(pkg, A_host, B_host, N, sample, phi):
-    """The CPU port of the reference's algorithm (oracle/, C + OpenMP, all host threads) on a sample block of the same
-    workload: rows [0, s) of A and columns [0, s) of B with the full K, N planes forced to the GPU run's N."""
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle  # noqa: E402  (timed CPU baseline; not part of the product path)
+    import oracle  # noqa: E402  (the CPU port: timed baseline and reference arm only, never the product path)
     oracle.build()
-    As = np.ascontiguousarray(A_host[:sample])
-    Bs = np.ascontiguousarray(B_host[:, :sample])
-    oracle.run(As[:8], Bs[:, :32], force_N=N)       # warm the thread pool
+    return oracle
+
+
+def oracle_decision(oracle, A_host, B_host, force_N=None):
+    """The reference algorithm's own decision on the workload's FULL inputs (CPU port, untimed): statistics over all
+    of A and B, the probe set and probe product, the rule -> (statistics, N, p)."""
+    m, k = A_host.shape
+    n = B_host.shape[1]
+    st = oracle.stats(A_host, B_host, True)
+    I, J = oracle.probe_sets(st, m, n, k, 0)
+    D = oracle.probe_D(A_host, B_host, I, J) if not force_N else np.zeros((len(I), len(J)))
+    ru = oracle.rule(st, m, n, k, I, J, D, force_N=force_N)
+    return st, ru["N"], ru["p"]
+
+
+def cpu_step(oracle, A_host, B_host, st, N, p, s):
+    """One CPU step on the sample block rows [0, s) x columns [0, s), full K: the block's statistics (timed work of
+    the step) and the core (split, exact INT8 products, CRT reconstruction) at the workload's own (N, p) and global
+    scalings, so the planes are those of the full product.  Returns seconds."""
+    As = np.ascontiguousarray(A_host[:s])
+    Bs = np.ascontiguousarray(B_host[:, :s])
+    sub = {"gam": st["gam"], "r": st["r"][:s], "c": st["c"][:s]}
     t0 = time.perf_counter()
-    C, info = oracle.run(As, Bs, force_N=N)
-    t = time.perf_counter() - t0
-    k = As.shape[1]
+    oracle.stats(As, Bs, True)
+    oracle.core(As, Bs, sub, N, p)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(oracle, A_host, B_host, st, N, p, sample, phi):
+    """The CPU port of the reference's algorithm (oracle/, C + OpenMP, all host threads) on a sample block of the
+    same workload (``cpu_step``), best of one timed step after a small warm-up."""
+    k = A_host.shape[1]
+    cpu_step(oracle, A_host[:8], B_host[:, :32], st, N, p, 8)          # warm the thread pool
+    t = cpu_step(oracle, A_host, B_host, st, N, p, sample)
     return {"value": 2.0 * sample * sample * k / t / 1e12, "unit": "TFLOPS", "cores": oracle.num_threads(),
             "kind": "port", "seconds": t,
-            "sample": f"rows 0..{sample} of A x columns 0..{sample} of B, full K={k}, N={N} forced, phi={phi}; "
-                      "stats + split + exact INT8 products + CRT reconstruction"}
+            "sample": f"rows 0..{sample} of A x columns 0..{sample} of B, full K={k}, phi={phi}, the full product's "
+                      f"N={N}, p={p} and scalings; block statistics + split + exact INT8 products + CRT "
+                      "reconstruction"}
 
 
 def auto_sample(k, N, threads):
@@ -178,35 +221,38 @@ def auto_sample(k, N, threads):
 
 # ------------------------------------------------------------------------------------------------ reference arm
 def run_reference(args):
+    """The reference arm: the reference's algorithm on the host cores (the C/OpenMP port in oracle/; the reference
+    itself has no CPU engine and its GPU path needs Windows DLLs).  The plane count and p are the rule's own answer on
+    the workload's full inputs, exactly as our arm decides them; each step is ``cpu_step`` on a sample block."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     pkg = __graft_entry__.load_package()
     m, k, n, phi, alt, forceN, desc = pkg.CONFIGS[args.workload]
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle  # noqa: E402
-    oracle.build()
+    if args.planes:
+        forceN = args.planes
+    oracle = _oracle()
     threads = oracle.num_threads()
-    N = forceN or {"c1": 16, "c2": 16, "c3": 19, "c4": 16}.get(args.workload, 16)
+    A, B = pkg.make_inputs(m, k, n, phi, 0, alt)
+    st, N, p = oracle_decision(oracle, A, B, forceN)
     s = args.cpu_sample or auto_sample(k, N, threads) // 2
-    # the sample block of the workload: the same generator, only the rows / columns that are used
-    A, B = pkg.make_inputs(m if m * k <= (1 << 28) else s, k, n if k * n <= (1 << 28) else s, phi, 0, alt)
-    As, Bs = np.ascontiguousarray(A[:s]), np.ascontiguousarray(B[:, :s])
     times = []
     for it in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        oracle.run(As, Bs, force_N=N)
-        dt = time.perf_counter() - t0
+        dt = cpu_step(oracle, A, B, st, N, p, s if it >= args.warmup else min(s, 64))
         if it >= args.warmup:
             times.append(dt)
     t = float(np.mean(times))
     v = 2.0 * s * s * k / t / 1e12
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    from matrix_numbers_b200.distributed import default_grid
+    grid = default_grid(world) if world > 1 else (1, 1)
     line = {"metric": METRIC, "value": v, "unit": "TFLOPS", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f64 (int8 residue arithmetic)", "data": "synthetic", "impl": "reference",
-            "config": {"workload": args.workload, "desc": desc, "m": m, "n": n, "k": k, "planes": N},
+            "config": workload_config(args, m, n, k, phi, N, p, world, grid),
             "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": threads, "kind": "port",
-                             "sample": f"rows 0..{s} x cols 0..{s} of the {args.workload} product, full K={k}, N={N}"},
+                             "sample": f"rows 0..{s} x cols 0..{s} of the {args.workload} product, full K={k}, the "
+                                       f"rule's N={N}, p={p} on the full inputs (block statistics + core per step)"},
             "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -253,6 +299,62 @@ def bench_chain(args):
 
 
 # ------------------------------------------------------------------------------------------------ our arm
+def timed_calls(torch, dist, call, steps, warmup, world, stream, clocks_rank=None, clock_log=None, stage_events=False):
+    """W untimed calls, then K calls bracketed by synchronize (+ barrier) and CUDA events on the launching stream;
+    returns (seconds per call, max over ranks; last info; per-stage seconds of this rank; clock summary or None)."""
+    info = None
+    for _ in range(warmup):
+        _, info = call(None)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    per_step = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(clocks_rank, clock_log) if clocks_rank is not None else None
+    if sampler is not None:
+        sampler.__enter__()
+        time.sleep(0.3)
+    try:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0.record(stream)
+        for _ in range(steps):
+            ev = [] if stage_events else None
+            _, info = call(ev)
+            if ev:
+                per_step.append(ev)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    finally:
+        if sampler is not None:
+            sampler.__exit__(None, None, None)
+    t = e0.elapsed_time(e1) / 1e3 / steps
+    if world > 1:
+        tt = torch.tensor([t], dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    stages = {}
+    for ev in per_step:
+        for (_, a), (name, b) in zip(ev[:-1], ev[1:]):
+            stages[name] = stages.get(name, 0.0) + a.elapsed_time(b) / 1e3 / len(per_step)
+    return t, info, stages, (sampler.summary() if sampler is not None else None)
+
+
+def stages_over_ranks(torch, dist, stages, world):
+    """Per-stage milliseconds of every rank (all_gather of this rank's figures; same stage names on all ranks)."""
+    names = list(stages)
+    if world == 1:
+        return {"rank0": {n_: stages[n_] * 1e3 for n_ in names}}
+    v = torch.tensor([stages[n_] * 1e3 for n_ in names], dtype=torch.float64, device="cuda")
+    out = torch.empty(world * len(names), dtype=torch.float64, device="cuda")
+    dist.all_gather_into_tensor(out, v)
+    out = out.view(world, len(names)).cpu().tolist()
+    return {f"rank{r}": dict(zip(names, out[r])) for r in range(world)}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -276,33 +378,23 @@ def main():
     m, k, n, phi, alt, forceN, desc = pkg.CONFIGS[args.workload]
     if args.planes:
         forceN = args.planes
+    stream = torch.cuda.current_stream()
+    clock_log = args.clock_log.replace(".csv", f"_rank{rank}.csv") if args.clock_log else None
 
-    # inputs: generated on the host (numpy, seed 0); rank a S + b of the R x S grid holds A's row block a and B's
-    # column block b (R = world, S = 1 for a plain row split)
+    # inputs: generated on the host (numpy, seed 0)
     t_gen = time.perf_counter()
     A_host, B_host = pkg.make_inputs(m, k, n, phi, 0, alt)
-    from matrix_numbers_b200.distributed import default_grid
-    R, S = default_grid(world) if world > 1 else (1, 1)
-    ga, gb = divmod(rank, S)
-    rows, cols = m // R, n // S
-    assert rows % 4 == 0 and cols % 32 == 0, "block shape rule"
-    r0, c0 = ga * rows, gb * cols
-    A_blk = A_host[r0:r0 + rows]
-    B_blk = np.ascontiguousarray(B_host[:, c0:c0 + cols]) if S > 1 else B_host
-    A = torch.from_numpy(A_blk).to(dev)
-    B = torch.from_numpy(B_blk).to(dev)
-    C = torch.empty((rows, cols), dtype=torch.float64, device=dev)
     t_gen = time.perf_counter() - t_gen
-
-    step_events = []
     products = 1
-    if world > 1:
-        assert args.mode in ("sampled", "certified"), "--mode config / persist are single-GPU"
-        E = pkg.DistributedOzakiCRT(grid=(R, S))
-        cert = args.mode == "certified"
-        call = lambda ev=None: E.run(A, B, C, force_N=forceN, certify=cert)  # noqa: E731
-    else:
+    extra = {}
+    if world == 1:
+        R, S = 1, 1
+        rows, cols = m, n
+        A = torch.from_numpy(A_host).to(dev)
+        B = torch.from_numpy(B_host).to(dev)
+        C = torch.empty((m, n), dtype=torch.float64, device=dev)
         E = pkg.OzakiCRT()
+        engine = E
         call = lambda ev=None: E.run_fast(A, B, C, force_N=forceN, events=ev)  # noqa: E731
         if args.mode == "certified":
             call = lambda ev=None: E.run_fast(A, B, C, events=ev, certify=True)  # noqa: E731
@@ -319,169 +411,176 @@ def main():
                 for _ in range(args.q):
                     PA.product(B, C)
                 return C, {"N": PA.N, "p": PA.p}
+        launches_of = lambda: E.launches  # noqa: E731
+    else:
+        # headline on N GPUs: C row blocks; A's and C's row blocks live on their owners, B lives on rank 0 only and
+        # is broadcast (FP64) over NCCL inside every timed call
+        assert args.mode in ("sampled", "certified"), "--mode config / persist are single-GPU"
+        cert = args.mode == "certified"
+        R, S = world, 1
+        rows, cols = m // R, n
+        assert rows % 4 == 0, "block shape rule"
+        A = torch.from_numpy(np.ascontiguousarray(A_host[rank * rows:(rank + 1) * rows])).to(dev)
+        B_root = torch.from_numpy(B_host).to(dev) if rank == 0 else None
+        C = torch.empty((rows, n), dtype=torch.float64, device=dev)
+        D = pkg.DistributedOzakiCRT(grid=(R, S))
+        engine = D.engine
+        call = lambda ev=None: D.run_broadcast_b(A, B_root, C, root=0, force_N=forceN, certify=cert, events=ev)  # noqa: E731
+        launches_of = lambda: D.launches  # noqa: E731
 
-    for _ in range(args.warmup):
-        _, info = call()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    launches0 = E.launches
-    stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clk_path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else None
-    with ClockSampler(local, clk_path) as clocks:
-        time.sleep(0.3)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e0.record(stream)
-        for _ in range(args.steps):
-            ev = [] if world == 1 else None
-            _, info = call(ev)
-            if ev:
-                step_events.append(ev)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-    t_dev = e0.elapsed_time(e1) / 1e3 / args.steps
-    launches = E.launches - launches0
-    if world > 1:
-        tt = torch.tensor([t_dev], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_dev = float(tt.item())
+    launches0 = launches_of()
+    t_dev, info, stages, clocks = timed_calls(torch, dist, call, args.steps, args.warmup, world, stream,
+                                              clocks_rank=local, clock_log=clock_log, stage_events=True)
+    launches = launches_of() - launches0
     flops = 2.0 * m * n * k * products
     value = flops / t_dev / 1e12
+    stage_ms = stages_over_ranks(torch, dist, stages, world)
 
-    # stage times inside the timed calls (CUDA events between the parts of run_fast)
-    in_step = {}
-    for ev in step_events:
-        for (n0, a), (n1, b_) in zip(ev[:-1], ev[1:]):
-            in_step[n1] = in_step.get(n1, 0.0) + a.elapsed_time(b_) / len(step_events)
+    if world > 1:
+        # beside the headline: the same product with every operand pre-placed (no operand bytes on NVLink), on the
+        # default grid; and with A and B on rank 0 only (A scattered, B broadcast, C gathered into rank 0)
+        from matrix_numbers_b200.distributed import default_grid
+        gR, gS = default_grid(world)
+        ga, gb = divmod(rank, gS)
+        br, bc = m // gR, n // gS
+        A_g = torch.from_numpy(np.ascontiguousarray(A_host[ga * br:(ga + 1) * br])).to(dev)
+        B_g = torch.from_numpy(np.ascontiguousarray(B_host[:, gb * bc:(gb + 1) * bc])).to(dev)
+        C_g = torch.empty((br, bc), dtype=torch.float64, device=dev)
+        Dg = pkg.DistributedOzakiCRT(grid=(gR, gS))
+        cert = args.mode == "certified"
+        t_pre, _, st_pre, _ = timed_calls(
+            torch, dist, lambda ev=None: Dg.run(A_g, B_g, C_g, force_N=forceN, certify=cert, events=ev),
+            args.steps, args.warmup, world, stream, stage_events=True)
+        extra["presharded"] = {"value": flops / t_pre / 1e12, "ms_per_step": t_pre * 1e3,
+                               "grid": f"{gR} x {gS} grid of C blocks",
+                               "what": "A's row blocks and B's column blocks already on their ranks; only the "
+                                       "statistics vectors and the probe product cross NVLink",
+                               "stages_ms": stages_over_ranks(torch, dist, st_pre, world)}
+        del A_g, B_g, C_g, Dg
+        A_root = torch.from_numpy(A_host).to(dev) if rank == 0 else None
+        C_root = torch.empty((m, n), dtype=torch.float64, device=dev) if rank == 0 else None
+        t_root, _, st_root, _ = timed_calls(
+            torch, dist,
+            lambda ev=None: D.run_from_root(A_root, B_root, C_root, root=0, force_N=forceN, certify=cert, events=ev),
+            args.steps, args.warmup, world, stream, stage_events=True)
+        extra["from_root"] = {"value": flops / t_root / 1e12, "ms_per_step": t_root * 1e3,
+                              "what": "A and B on rank 0 only: A's row blocks scattered, B broadcast, C's row "
+                                      "blocks gathered into rank 0, all inside the timed call",
+                              "stages_ms": stages_over_ranks(torch, dist, st_root, world)}
+        del A_root, C_root
+        torch.cuda.empty_cache()
+        # the exchange that limits the headline: the largest stage time of a collective step, over ranks
+        coll = [x for x in next(iter(stage_ms.values())) if x != "core"]
+        worst = max(((r_, x, v) for r_, d in stage_ms.items() for x, v in d.items() if x in coll),
+                    key=lambda z: z[2], default=None)
+        extra["limiting_collective"] = None if worst is None else {"stage": worst[1], "rank": worst[0],
+                                                                   "ms": worst[2]}
 
     # roofline of the dominant kernel (the INT8 products with the fused reduction): live CUDA-event time per launch
     Nplanes = info.get("N") or forceN
     prof = {}
-    engine = E.engine if world > 1 else E
     b = engine.buffers(rows, cols, k, Nplanes)
+    B_core = B if world == 1 else D._recv.get("B", B_root)
     for _ in range(3):
-        engine.core(A, B, b, Nplanes, C, prof=prof)
+        engine.core(A, B_core, b, Nplanes, C, prof=prof)
     t_gemm = prof["gemm+reduce"] / 3
     int8_ops = 2.0 * Nplanes * rows * cols * k
     peak_int8 = int8_peak_tops(torch, dev)
     hbm_peak, bf16_peak, peak_src = measured_peaks()
     achieved = int8_ops / t_gemm / 1e12
+    has_traffic = world == 1 and args.mode == "sampled" and args.workload in GEMM_TRAFFIC_BYTES
     roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel<residue> (tcgen05.mma kind::i8)", "achieved": achieved,
                 "peak": peak_int8, "unit": "TOPS (INT8)", "frac": achieved / peak_int8,
                 "peak_source": "cuBLASLt INT8 GEMM 8192^3 burst measured in this run (torch._int_mm)",
                 "bf16_measured_tflops_x2": 2 * bf16_peak, "frac_of_2x_bf16": achieved / (2 * bf16_peak),
-                "traffic": GEMM_TRAFFIC_BYTES.get(args.workload) if world == 1 and args.mode == "sampled" else None,
+                "traffic": GEMM_TRAFFIC_BYTES[args.workload] if has_traffic else None,
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                "traffic_source": GEMM_TRAFFIC_SOURCE.format(w=args.workload) if has_traffic else None,
                 "algorithmic_ops_per_launch": int8_ops, "ms_per_launch": t_gemm * 1e3,
-                "stages_ms": {k_: v * 1e3 / 3 for k_, v in prof.items()}, "timed_call_stages_ms": in_step}
+                "stages_ms": {k_: v * 1e3 / 3 for k_, v in prof.items()}, "timed_call_stages_ms": stage_ms}
     # the emulated-FP64 ceiling is the INT8 rate over the plane count (one INT8 product per plane); the residue split
-    # moves (8 + N)(rows k + k cols) bytes (FP64 in, N planes out) against the measured copy bandwidth
-    t_split = prof["residues"] / 3
+    # moves (8 + N)(rows k + k cols) bytes (FP64 in, N planes out) and the reconstruction (N + 8) rows cols bytes
+    t_split, t_recon = prof["residues"] / 3, prof["recon"] / 3
     split_bytes = (8.0 + Nplanes) * (rows * k + k * cols)
+    recon_bytes = (8.0 + Nplanes) * rows * cols
     roofline["emulated_ceiling_tflops"] = peak_int8 / Nplanes
     roofline["frac_of_int8_over_N"] = (2.0 * rows * cols * k / (t_dev / products) / 1e12) / (peak_int8 / Nplanes)
     roofline["split"] = {"bound": "hbm", "achieved": split_bytes / t_split / 1e9, "peak": hbm_peak, "unit": "GB/s",
                          "frac": split_bytes / t_split / 1e9 / hbm_peak, "bytes_per_call": split_bytes}
+    roofline["recon"] = {"bound": "hbm", "achieved": recon_bytes / t_recon / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": recon_bytes / t_recon / 1e9 / hbm_peak, "bytes_per_call": recon_bytes}
 
     # accuracy on a sample (rank 0's block): E1 / E2 against the correctly rounded product, native DGEMM beside it
     acc = None
     if rank == 0 and not args.no_accuracy:
-        Cn = A @ B
+        Cn = A @ B_core
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
-        torch.matmul(A, B, out=Cn)
+        torch.matmul(A, B_core, out=Cn)
         t1.record()
         torch.cuda.synchronize()
         t_nat = t0.elapsed_time(t1) / 1e3
-        Smp = pkg.Sample(A, B, Cn, nr=24, nc=24)
+        Smp = pkg.AccuracySample(A, B_core, Cn, nr=24, nc=24)
         acc = {"engine": Smp.errors(C), "native_dgemm": Smp.errors(Cn),
-               "native_dgemm_tflops": 2.0 * rows * cols * k / t_nat / 1e12}
+               "native_dgemm_tflops": 2.0 * rows * cols * k / t_nat / 1e12,
+               "native_dgemm_shape": [rows, cols, k]}
         del Cn
 
     # end to end through the public API with host buffers (pinned), H2D + D2H inside the timed region
     e2e = None
     if args.e2e_steps > 0:
-        Ah = torch.from_numpy(A_blk).pin_memory()
-        Bh = torch.from_numpy(B_blk).pin_memory()
+        Ah = torch.from_numpy(np.ascontiguousarray(A_host[rank * rows:(rank + 1) * rows])).pin_memory()
+        Bh = torch.from_numpy(B_host).pin_memory() if (world == 1 or rank == 0) else None
         Ch = torch.empty((rows, cols), dtype=torch.float64).pin_memory()
-        call()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        host_api = world == 1 and args.mode == "sampled"
-        if host_api:
-            E.run_host(Ah, Bh, Ch, force_N=forceN)          # warm-up of the host-buffer path
+        if world == 1 and args.mode == "sampled":
+            E.run_host(Ah, Bh, Ch, force_N=forceN)             # warm-up of the host-buffer path
             torch.cuda.synchronize()
-        f0.record(stream)
-        for _ in range(args.e2e_steps):
-            if host_api:
-                # the public host-buffer call: H2D of A and B, the product, D2H of C overlapped block by block
-                E.run_host(Ah, Bh, Ch, force_N=forceN)
-            else:
-                A.copy_(Ah, non_blocking=True)
-                B.copy_(Bh, non_blocking=True)
-                call()
-                Ch.copy_(C, non_blocking=True)
-        f1.record(stream)
-        torch.cuda.synchronize()
-        t_e2e = f0.elapsed_time(f1) / 1e3 / args.e2e_steps
-        if world > 1:
-            tt = torch.tensor([t_e2e], dtype=torch.float64, device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            t_e2e = float(tt.item())
-        e2e = {"value": flops / t_e2e / 1e12, "unit": "TFLOPS", "ms_per_step": t_e2e * 1e3,
-               "api": "OzakiCRT.run_host (host buffers)" if host_api else "device run between host copies",
-               "h2d_bytes_per_step": (Ah.numel() + Bh.numel()) * 8 * world, "d2h_bytes_per_step": Ch.numel() * 8 * world}
-        if world > 1:
-            # the same stream of products through DistributedOzakiCRT.run_host_many on every rank
-            cert = args.mode == "certified"
-            E.run_host_many([(Ah, Bh, Ch)] * 2, force_N=forceN, certify=cert)
-            torch.cuda.synchronize()
-            dist.barrier()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             f0.record(stream)
-            E.run_host_many([(Ah, Bh, Ch)] * args.e2e_steps, force_N=forceN, certify=cert)
+            for _ in range(args.e2e_steps):
+                E.run_host(Ah, Bh, Ch, force_N=forceN)
             f1.record(stream)
             torch.cuda.synchronize()
-            tt = torch.tensor([f0.elapsed_time(f1) / 1e3 / args.e2e_steps], dtype=torch.float64, device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            t_many = float(tt.item())
-            e2e_single = e2e
-            e2e = {"value": flops / t_many / 1e12, "unit": "TFLOPS", "ms_per_step": t_many * 1e3,
-                   "api": f"DistributedOzakiCRT.run_host_many ({args.e2e_steps} products per rank; each step's H2D of "
-                          "the rank's blocks, product and D2H of its C block inside the timed region, the next step's "
-                          "H2D overlapped with this step's product)",
-                   "h2d_bytes_per_step": e2e_single["h2d_bytes_per_step"],
-                   "d2h_bytes_per_step": e2e_single["d2h_bytes_per_step"], "single_call": e2e_single}
-        if host_api:
-            # a stream of e2e_steps products through OzakiCRT.run_host_many: every step still copies its A and B in
-            # and its C out, but the next step's H2D runs while this step computes (the pipeline fill is included)
+            t_single = f0.elapsed_time(f1) / 1e3 / args.e2e_steps
             E.run_host_many([(Ah, Bh, Ch)] * 2, force_N=forceN)   # warm-up of the second slot
             torch.cuda.synchronize()
             f0.record(stream)
             E.run_host_many([(Ah, Bh, Ch)] * args.e2e_steps, force_N=forceN)
             f1.record(stream)
             torch.cuda.synchronize()
-            t_many = f0.elapsed_time(f1) / 1e3 / args.e2e_steps
-            e2e_single = e2e
-            e2e = {"value": flops / t_many / 1e12, "unit": "TFLOPS", "ms_per_step": t_many * 1e3,
-                   "api": f"OzakiCRT.run_host_many (host buffers, {args.e2e_steps} products; each step's H2D, product "
-                          "and D2H inside the timed region, the next step's H2D overlapped with this step's product)",
-                   "h2d_bytes_per_step": e2e_single["h2d_bytes_per_step"],
-                   "d2h_bytes_per_step": e2e_single["d2h_bytes_per_step"], "single_call": e2e_single}
+            t_e2e = f0.elapsed_time(f1) / 1e3 / args.e2e_steps
+            api = (f"OzakiCRT.run_host_many (host buffers, {args.e2e_steps} products; each step's H2D, product and "
+                   "D2H inside the timed region, the next step's H2D overlapped with this step's product)")
+            single = {"value": flops / t_single / 1e12, "ms_per_step": t_single * 1e3,
+                      "api": "OzakiCRT.run_host (one call at a time)"}
+        else:
+            # every step: H2D of this rank's A rows (and of B on rank 0), the headline call, D2H of the C rows
+            def host_step(ev=None):
+                A.copy_(Ah, non_blocking=True)
+                if world > 1 and rank == 0:
+                    B_root.copy_(Bh, non_blocking=True)
+                elif world == 1:
+                    B.copy_(Bh, non_blocking=True)
+                out = call(None)
+                Ch.copy_(C, non_blocking=True)
+                return out
+            t_e2e, _, _, _ = timed_calls(torch, dist, host_step, args.e2e_steps, 1, world, stream)
+            api = ("per rank: H2D of its A rows (rank 0 also B), DistributedOzakiCRT.run_broadcast_b, D2H of its C "
+                   "rows" if world > 1 else "H2D of A and B, OzakiCRT.run_fast, D2H of C")
+            single = None
+        e2e = {"value": flops / t_e2e / 1e12, "unit": "TFLOPS", "ms_per_step": t_e2e * 1e3, "api": api,
+               "h2d_bytes_per_step": (m * k + k * n) * 8, "d2h_bytes_per_step": m * n * 8}
+        if single is not None:
+            e2e["single_call"] = single
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle  # noqa: E402
-        s = args.cpu_sample or auto_sample(k, Nplanes, oracle.num_threads())
-        cpu = cpu_baseline(pkg, A_host, B_host, Nplanes, s, phi)
+        oracle = _oracle()
+        st_full, N_o, p_o = oracle_decision(oracle, A_host, B_host, forceN)
+        s = args.cpu_sample or auto_sample(k, N_o, oracle.num_threads())
+        cpu = cpu_baseline(oracle, A_host, B_host, st_full, N_o, p_o, s, phi)
+        cpu["decision_equals_gpu"] = bool((N_o, p_o) == (Nplanes, info.get("p")))
 
     if world > 1:
         dist.barrier()
@@ -490,12 +589,14 @@ def main():
         line = {"metric": metric, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": t_dev * 1e3, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f64 (int8 residue arithmetic)", "data": "synthetic",
-                "config": {"workload": args.workload, "desc": desc, "m": m, "n": n, "k": k, "phi": phi,
-                           "planes": Nplanes, "p": info.get("p"), "mode": args.mode, "products_per_step": products,
-                           "parallelism": f"{R} x {S} grid of C blocks" if world > 1 else "single GPU",
-                           "l2": "inputs larger than L2 (2 x 2.1 GB fp64)", "input_generation_s": t_gen},
-                "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "accuracy": acc, "clocks": clocks.summary(),
+                "config": workload_config(args, m, n, k, phi, Nplanes, info.get("p"), world, (R, S), products),
+                "input_generation_s": t_gen,
+                "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "accuracy": acc, "clocks": clocks,
                 "gpu_launches": launches, "hbm_peak_gbs": hbm_peak, "peaks": peak_src}
+        if world > 1:
+            line["operands"] = ("A's and C's row blocks on their ranks; B on rank 0, broadcast (FP64) over NCCL "
+                                "inside every timed call")
+            line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

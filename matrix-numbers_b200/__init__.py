@@ -35,13 +35,15 @@ def __getattr__(name):
     if name in ("coprime_ip", "int8_crt", "chain_cost_model"):
         from . import planning
         return getattr(planning, name)
-    if name in ("make_inputs", "make_inputs_w", "config_inputs", "Sample", "exact_sample", "audit_bound", "CONFIGS"):
-        from . import harness
-        return getattr(harness, name)
+    if name in ("make_inputs", "make_inputs_w", "config_inputs", "Sample", "exact_sample", "audit_bound", "CONFIGS",
+                "AccuracySample", "correctly_rounded_products", "two_products"):
+        from . import measure
+        return getattr(measure, name)
     raise AttributeError(name)
 
 
 __all__ = ["OzakiCRT", "DistributedOzakiCRT", "PersistA", "full_certificate", "MODS", "NMAX", "NEG", "pmax_bits", "bound_matrix", "worst_case_p",
            "sigma_of", "make_config_table", "pick_config", "limbs_for", "_limbs_for", "_pow2tab", "modulus_product",
-           "make_inputs", "make_inputs_w", "config_inputs", "Sample", "exact_sample", "audit_bound", "CONFIGS", "coprime_ip", "int8_crt",
+           "make_inputs", "make_inputs_w", "config_inputs", "Sample", "exact_sample", "audit_bound", "CONFIGS",
+           "AccuracySample", "correctly_rounded_products", "two_products", "coprime_ip", "int8_crt",
            "chain_cost_model", "ResidueChain", "planes_for", "chain_bound", "_lib"]

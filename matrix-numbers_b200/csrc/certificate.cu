@@ -355,10 +355,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const float vf = __uint_as_float(v[e]);
                         const float sf = aI + bs[e];
                         const float den = __fmaf_rn(__fmul_rn(sf, sf), 4.0f, __fmul_rn(cp.k4, vf));
-                        const float L = __fmul_rn(__fmul_rn(__fmul_rn(vf, sf), rcp_approx_f32(den)), cp.c8);
+                        const float q = __fmul_rn(__fmul_rn(vf, sf), rcp_approx_f32(den));
+                        const float L = __fmul_rn(q, cp.c8);
                         const bool in_range = sf == sf;
                         const bool pos = vf > 0.0f;
-                        const bool above = L >= best_up && L >= 0x1p-100f && L < INFINITY;
+                        // q must be a normal FP32 number: a subnormal q carries only a few bits and may be rounded
+                        // up by far more than the 2^-8 margin (in the proven range that only happens where L is
+                        // far below xmax, but the check keeps the argument local)
+                        const bool above = L >= best_up && L >= 0x1p-100f && L < INFINITY && q >= 0x1p-126f;
                         zero |= (in_range && !pos) ? (1u << e) : 0u;
                         keep |= (in_range && (!pos || above)) ? 0u : (1u << e);
                     }

@@ -7,6 +7,7 @@
 //     atomicAdd (:949-950), whose order varies from run to run;
 //   - loads are 16-byte vectors, coalesced along the contiguous index of each matrix.
 #include "ozk_common.cuh"
+#include <atomic>
 
 namespace {
 
@@ -387,7 +388,9 @@ namespace {
 
 __device__ __align__(256) unsigned char g_stats_scratch[OZK_STATS_NOALLOC_MAX_BYTES];
 
-void* g_stats_scratch_ptr[64];   // device address of g_stats_scratch, per device ordinal (set up on first use)
+// device address of g_stats_scratch, per device ordinal (set up on first use); atomic because several host threads
+// may make their first call at once (they all store the same address)
+std::atomic<void*> g_stats_scratch_ptr[64];
 
 }  // namespace
 
@@ -399,14 +402,14 @@ extern "C" int ozk_stats_noalloc(const double* A, const double* B, int m, int n,
     if (need > (size_t)OZK_STATS_NOALLOC_MAX_BYTES) return OZK_ERR_TOO_LARGE;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return OZK_ERR_DEVICE;
-    if (!g_stats_scratch_ptr[dev]) {
+    void* scratch = g_stats_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (!scratch) {
         // one-time set-up on this device (the current one): the host-side name of the array is not a device address
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_stats_scratch);
-        if (e != cudaSuccess || !p) return OZK_ERR_CUDA_BASE + (int)e;
-        g_stats_scratch_ptr[dev] = p;
+        const cudaError_t e = cudaGetSymbolAddress(&scratch, g_stats_scratch);
+        if (e != cudaSuccess || !scratch) return OZK_ERR_CUDA_BASE + (int)e;
+        g_stats_scratch_ptr[dev].store(scratch, std::memory_order_relaxed);
     }
     // the statistics clear what must start at zero (the column maxima, the flag); everything else is overwritten
-    return ozk_stats(A, B, m, n, k, inside, gam, r, c, sA, nA, sB, nB, flag, g_stats_scratch_ptr[dev],
+    return ozk_stats(A, B, m, n, k, inside, gam, r, c, sA, nA, sB, nB, flag, scratch,
                      (size_t)OZK_STATS_NOALLOC_MAX_BYTES, stream);
 }

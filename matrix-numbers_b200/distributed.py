@@ -21,6 +21,19 @@ like the values) gives the minimum over all of C, and one all_reduce(SUM) the un
 the certified-mode decision from the same numbers.  The result equals the single-GPU product bit for bit (same gamma, r, c, N, p;
 the CRT stage is exact).
 
+Where the operands start.  ``run`` takes pre-placed blocks (each rank already holds its rows of A and its columns of
+B).  Two more entry points move the operands over NCCL inside the call, on a row-block grid (S = 1):
+
+* ``run_broadcast_b`` -- A's and C's row blocks live on their owners; B lives on one root rank and is broadcast as
+  FP64 (k n 8 bytes) before the statistics.  Broadcasting the FP64 operand moves fewer bytes than its N residue
+  planes would (N k n, N = 16-20), and every rank splits B itself.
+* ``run_from_root`` -- A, B (and C) live on the root only: A's row blocks are scattered, B broadcast, and (with
+  ``gather=True``) the row blocks of C gathered back into the root's C.
+
+Every collective is NCCL's (no peer-memory loads, no TMA multicast): the exchanges are plain operand moves and small
+statistics vectors, with no computation to fuse them with.  ``events`` (a list) receives (name, CUDA event) marks
+after each phase, for per-stage timing on each rank.
+
 Compute is delegated to an ``ops`` object: ``CudaOps`` (default) calls libozaki_b200.so on the rank's GPU; the CPU
 tests substitute an implementation with the same interface to check the orchestration over gloo ranks.
 """
@@ -47,6 +60,7 @@ class CudaOps:
     def __init__(self):
         from .engine import OzakiCRT
         self.engine = OzakiCRT()
+        self.timed = True                                     # phases can be marked with CUDA events
         self.lib = self.engine.lib
         self.device = torch.device("cuda", torch.cuda.current_device())
         self._glob = {}
@@ -130,8 +144,8 @@ class CudaOps:
                                        h["k"], float(tau), float(safety), ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]),
                                        ptr(h["ws"]), h["ws"].numel(), self._stream()), "ozk_rule_finish")
         self.engine.launches += 2
-        ctl, aux = self.engine._read_ctl(b)
-        return ctl[0], ctl[1], ctl[2], ctl[3], aux
+        dec, _, aux = b.fetch()
+        return dec.N, dec.p, int(dec.fallback), dec.p_req, aux
 
     def certificate_block(self, A, B, st, tau, safety):
         """This block's minimum xmax (float64 bit pattern as int64, -1 when no entry has D > 0) and its uncertified
@@ -149,10 +163,10 @@ class CudaOps:
                                           ptr(b["dec"]), ptr(b["pdev"]), ptr(b["aux"]), self._stream()),
               "ozk_rule_certified")
         self.engine.launches += 1
-        ctl, aux = self.engine._read_ctl(b)
+        dec, _, _ = b.fetch()
         if int(self._cert["err"].item()):
             raise _lib.OzkError(f"ozk_certificate: device error flag {int(self._cert['err'].item()):#x}")
-        return ctl[0], ctl[1], ctl[2], ctl[3]
+        return dec.N, dec.p, int(dec.fallback), dec.p_req
 
     def core(self, A, B, st, N, p, C):
         rows, k = A.shape
@@ -185,6 +199,7 @@ class DistributedOzakiCRT:
         self.a, self.b = divmod(self.rank, self.S)
         self.ops = ops if ops is not None else CudaOps()
         self.probe = {}
+        self._recv = {}                                       # receive buffers of the operand moves, per name
 
     @property
     def engine(self):
@@ -212,8 +227,79 @@ class DistributedOzakiCRT:
         parts = parts.view(self.world, x.numel())
         return parts[0:stride * count:stride].reshape(total)
 
+    def _mark(self, events, name):
+        if events is not None and getattr(self.ops, "timed", False):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            events.append((name, e))
+
+    def _buffer(self, name, shape, dtype, device):
+        """A receive buffer kept between calls (replaced when the shape changes)."""
+        t = self._recv.get(name)
+        if t is None or tuple(t.shape) != tuple(shape) or t.dtype != dtype or t.device != device:
+            t = self._recv[name] = torch.empty(shape, dtype=dtype, device=device)
+        return t
+
+    def _header(self, values, root, device):
+        """Broadcast a few int64 sizes from the root (the other ranks pass placeholders)."""
+        h = torch.tensor(values, dtype=torch.int64, device=device)
+        dist.broadcast(h, src=root, group=self.group)
+        return [int(x) for x in h.tolist()]
+
+    def _device_of(self, *tensors):
+        for t in tensors:
+            if t is not None:
+                return t.device
+        return getattr(self.ops, "device", torch.device("cpu"))
+
+    def run_broadcast_b(self, A, B=None, C=None, root=0, events=None, **kw):
+        """This rank's row block of C = A B when B lives only on rank ``root``: B (k x n FP64) is broadcast from the
+        root over NCCL, then the blocks are multiplied as in ``run``.  A (rows x k) is this rank's row block; B is
+        the whole B on the root and ignored elsewhere.  Needs a row-block grid (S = 1)."""
+        assert self.S == 1, "run_broadcast_b needs a row-block grid (S = 1)"
+        dev = self._device_of(A, B)
+        k = A.shape[1]
+        k_b, n = self._header([B.shape[0], B.shape[1]] if self.rank == root else [0, 0], root, dev)
+        assert k_b == k, "A's and B's inner dimensions differ"
+        Bl = B if self.rank == root else self._buffer("B", (k, n), torch.float64, dev)
+        if self.rank == root:
+            assert B.is_contiguous() and B.dtype == torch.float64
+        self._mark(events, "start")
+        dist.broadcast(Bl, src=root, group=self.group)
+        self._mark(events, "broadcast B")
+        return self.run(A, Bl, C, events=events, **kw)
+
+    def run_from_root(self, A=None, B=None, C=None, root=0, gather=True, events=None, **kw):
+        """C = A B with A (m x k) and B (k x n) only on rank ``root``: A's row blocks are scattered, B broadcast,
+        each rank multiplies its block, and with ``gather`` the row blocks of C are gathered into the root's C
+        (allocated when None).  Returns (C on the root -- this rank's row block elsewhere or without gather, info).
+        Needs a row-block grid (S = 1) and m divisible by the number of ranks."""
+        assert self.S == 1, "run_from_root needs a row-block grid (S = 1)"
+        dev = self._device_of(A, B, C)
+        m, k, n = self._header(list(A.shape) + [B.shape[1]] if self.rank == root else [0, 0, 0], root, dev)
+        assert m % self.R == 0, "m must divide into equal row blocks"
+        rows = m // self.R
+        Ab = self._buffer("A", (rows, k), torch.float64, dev)
+        Bl = B if self.rank == root else self._buffer("B", (k, n), torch.float64, dev)
+        Cb = self._buffer("C", (rows, n), torch.float64, dev)
+        if self.rank == root:
+            assert A.is_contiguous() and B.is_contiguous() and A.dtype == B.dtype == torch.float64
+            if C is None and gather:
+                C = torch.empty((m, n), dtype=torch.float64, device=dev)
+        self._mark(events, "start")
+        dist.scatter(Ab, list(A.split(rows)) if self.rank == root else None, src=root, group=self.group)
+        self._mark(events, "scatter A")
+        dist.broadcast(Bl, src=root, group=self.group)
+        self._mark(events, "broadcast B")
+        _, info = self.run(Ab, Bl, Cb, events=events, **kw)
+        if not gather:
+            return Cb, info
+        dist.gather(Cb, list(C.split(rows)) if self.rank == root else None, dst=root, group=self.group)
+        self._mark(events, "gather C")
+        return (C if self.rank == root else Cb), info
+
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, safety=2.0,
-            config=None, certify=False):
+            config=None, certify=False, events=None):
         if config is not None:
             force_N, force_p = int(config["N"]), config.get("p")
         rows, k = A.shape
@@ -228,6 +314,7 @@ class DistributedOzakiCRT:
         rm = self.ops.rowmax(B)
         mx = torch.cat([cm, rm])
         dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=self.group)
+        self._mark(events, "maxima + all_reduce")
         st = self.ops.local_stats(A, B, mx[:k], mx[k:], inside)
         # 2. statistics of all rows and columns
         glob = self.ops.global_stats(m, n, A.device)
@@ -235,6 +322,7 @@ class DistributedOzakiCRT:
             glob[x].copy_(self._gather(st[x], m, self.S, self.R))
         for x in ("c", "sB", "nB"):
             glob[x].copy_(self._gather(st[x], n, 1, self.S))
+        self._mark(events, "statistics + all_gather")
         if certify and force_N is None:
             # 3'. full-matrix certificate: minimum over the blocks, then the same decision everywhere
             xb, unc = self.ops.certificate_block(A, B, st, tau, safety)
@@ -257,10 +345,12 @@ class DistributedOzakiCRT:
         D = self.ops.rule_probe(h, A, B, row_begin, col_begin)
         dist.all_reduce(D, op=dist.ReduceOp.SUM, group=self.group)
         N, p, fb, preq, aux = self.ops.rule_finish(h, glob, tau, safety)
+        self._mark(events, "rule (probe + all_reduce + host read)")
         if fb or N == 0:
             self.ops.native(A, B, C)
             return C, {"fallback": True, "preq": preq}
         self.ops.core(A, B, st, N, p, C)
+        self._mark(events, "core")
         return C, {"N": N, "p": p, "preq": preq, "rows": [row_begin, row_begin + rows],
                    "cols": [col_begin, col_begin + cols], "grid": [self.R, self.S], "world": self.world}
 

@@ -79,8 +79,8 @@ class PersistA:
 
     def last_decision(self):
         """(N, p, fallback) of the forced rule of the last product (synchronises)."""
-        ctl, _ = self.E._read_ctl(self.b)
-        return ctl[0], ctl[5], bool(ctl[2])
+        dec, words, _ = self.b.fetch()
+        return dec.N, int(words[5]), dec.fallback
 
 
 __all__ = ["PersistA"]

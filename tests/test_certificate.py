@@ -56,14 +56,51 @@ def test_fast_bound_is_below_the_formula():
             x = (2.0 * thr) / (F1 + np.sqrt(F1 * F1 + (4.0 * F2) * thr))
             s = (sA / rI).astype(f32) + (sB / cJ).astype(f32)
             den = (s * s) * f32(4.0) + f32(k4) * v32
-            L = ((v32 * s) * np.nextafter(f32(1.0) / den, f32(np.inf))) * f32(c8)
-        used = (L >= 2.0 ** -100) & np.isfinite(L)
+            q = (v32 * s) * np.nextafter(f32(1.0) / den, f32(np.inf))
+            L = q * f32(c8)
+        used = (L >= 2.0 ** -100) & np.isfinite(L) & (q >= f32(2.0 ** -126))
         ratio = L[used].astype(np.float64) / x[used]
         assert ratio.max() < 1.0
         if ext == 0:
             assert ratio.min() > 1.0 - 2.0 ** -7
         checked += int(used.sum())
     assert checked > 200000
+
+
+def test_fast_bound_small_terms_large_kappa():
+    """The corner where the bound's quotient q = v s / den leaves FP32's normal range: k4 = 4 k kap at the top of the
+    allowed range (2^110), row and column terms from 2^-59 up.  q is then subnormal or zero; the kernel does not skip
+    on a subnormal q, and every entry it would skip on has L below the reference's FP64 xmax."""
+    f32 = np.float32
+    rng = np.random.default_rng(5)
+    k = 262144
+    derate = 1.0 - 8.0 * k * 2.0 ** -24
+    tau = 2.0 ** -52
+    safety = tau * derate / 2.0 ** 90                     # kap = 2^90: k4 = 2^110, c8 ~ 2^93
+    kap = tau * derate / safety
+    c8, k4 = 8.0 * kap * (1 - 2.0 ** -8), 4.0 * k * kap
+    assert 2.0 ** -110 <= c8 <= 2.0 ** 110 and k4 <= 2.0 ** 110
+    n = 100000
+    subnormal_seen = 0
+    for e in range(-59, 61, 4):
+        a = np.exp2(e + rng.uniform(-1, 0, n))
+        b = np.exp2(rng.uniform(-59, e, n))
+        v32 = np.exp2(rng.uniform(-48, 31, n)).astype(f32)
+        v = v32.astype(np.float64)
+        with np.errstate(all="ignore"):
+            D = v * derate
+            thr = (tau * D) / safety
+            F1 = 0.5 * (b + a)
+            F2 = 0.25 * k
+            x = (2.0 * thr) / (F1 + np.sqrt(F1 * F1 + (4.0 * F2) * thr))
+            s = a.astype(f32) + b.astype(f32)
+            den = (s * s) * f32(4.0) + f32(k4) * v32
+            q = (v32 * s) * np.nextafter(f32(1.0) / den, f32(np.inf))
+            L = q * f32(c8)
+        subnormal_seen += int(((q > 0) & (q < f32(2.0 ** -126))).sum())
+        used = (L >= 2.0 ** -100) & np.isfinite(L) & (q >= f32(2.0 ** -126))
+        assert np.all(L[used].astype(np.float64) < x[used])
+    assert subnormal_seen > 0
 
 
 def _dev_stats(torch, E, Ad, Bd):

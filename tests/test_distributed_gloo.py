@@ -30,6 +30,7 @@ class OracleOps:
     def __init__(self, oracle):
         self.O = oracle
         self.launches = 0
+        self.device = torch.device("cpu")
 
     def colmax(self, A):
         return torch.from_numpy(self.O.colmax(A.numpy()).copy())
@@ -125,8 +126,24 @@ def _worker(rank, world, port, outdir, mode):
         D = DistributedOzakiCRT(ops=OracleOps(O), grid=(R, S))
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure on rank 1 before the first collective")
-        C, info = D.run(Al, Bt, certify=mode.startswith("cert"))
-        C2, info2 = D.run(Al, Bt, force_N=22)
+        if mode in ("bcastB", "root"):
+            # the operands start on rank 1 (the root): B only (A's rows on their owners), or A and B both
+            root = 1
+            Bfull = torch.from_numpy(B) if rank == root else None
+            if mode == "bcastB":
+                C, info = D.run_broadcast_b(Al, Bfull, root=root)
+                C2, info2 = D.run_broadcast_b(Al, Bfull, root=root, force_N=22)
+            else:
+                Afull = torch.from_numpy(A) if rank == root else None
+                C, info = D.run_from_root(Afull, Bfull, root=root)
+                C2, info2 = D.run_from_root(Afull, Bfull, root=root, force_N=22)
+                if rank != root:                 # every rank holds its row block; the root holds all of C
+                    C, C2 = torch.zeros(m, n, dtype=torch.float64), torch.zeros(m, n, dtype=torch.float64)
+                Cb, _ = D.run_from_root(Afull, Bfull, root=root, gather=False)
+                np.save(os.path.join(outdir, f"Cblock_{rank}.npy"), Cb.numpy())
+        else:
+            C, info = D.run(Al, Bt, certify=mode.startswith("cert"))
+            C2, info2 = D.run(Al, Bt, force_N=22)
         np.save(os.path.join(outdir, f"C_{rank}.npy"), C.numpy())
         np.save(os.path.join(outdir, f"C22_{rank}.npy"), C2.numpy())
         with open(os.path.join(outdir, f"info_{rank}.txt"), "w") as f:
@@ -190,6 +207,42 @@ def test_certified_blocks_equal_single_process(oracle, tmp_path, pkg, mode, worl
     infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(world)]
     assert all(i == infos[0] for i in infos)
     assert infos[0][:3] == (iref["N"], iref["p"], iref["p_req"])
+
+
+def test_broadcast_b_from_root_equals_single_process(oracle, tmp_path, pkg):
+    """A's and C's row blocks on their owners, B only on the root (rank 1): B is broadcast inside the call."""
+    alive = _spawn(2, "bcastB", tmp_path)
+    assert not any(alive)
+    errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    A, B = pkg.make_inputs(128, 256, 128, 2.0, seed=31)
+    Cref, iref = oracle.run(A, B)
+    C = np.concatenate([np.load(os.path.join(tmp_path, f"C_{r}.npy")) for r in range(2)])
+    np.testing.assert_array_equal(C.view(np.uint64), Cref.view(np.uint64))
+    C22ref, i22 = oracle.run(A, B, force_N=22)
+    C22 = np.concatenate([np.load(os.path.join(tmp_path, f"C22_{r}.npy")) for r in range(2)])
+    np.testing.assert_array_equal(C22.view(np.uint64), C22ref.view(np.uint64))
+    infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(2)]
+    assert infos[0] == infos[1] and infos[0][:3] == (iref["N"], iref["p"], iref["p_req"])
+
+
+def test_run_from_root_scatter_broadcast_gather(oracle, tmp_path, pkg):
+    """A and B only on the root (rank 1): A scattered by row blocks, B broadcast, C gathered into the root's C; and
+    without the gather every rank keeps its row block."""
+    alive = _spawn(2, "root", tmp_path)
+    assert not any(alive)
+    errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    A, B = pkg.make_inputs(128, 256, 128, 2.0, seed=31)
+    Cref, iref = oracle.run(A, B)
+    np.testing.assert_array_equal(np.load(os.path.join(tmp_path, "C_1.npy")).view(np.uint64), Cref.view(np.uint64))
+    C22ref, _ = oracle.run(A, B, force_N=22)
+    np.testing.assert_array_equal(np.load(os.path.join(tmp_path, "C22_1.npy")).view(np.uint64),
+                                  C22ref.view(np.uint64))
+    blocks = np.concatenate([np.load(os.path.join(tmp_path, f"Cblock_{r}.npy")) for r in range(2)])
+    np.testing.assert_array_equal(blocks.view(np.uint64), Cref.view(np.uint64))
+    infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(2)]
+    assert infos[0] == infos[1] and infos[0][:3] == (iref["N"], iref["p"], iref["p_req"])
 
 
 def test_failed_rank_ends_peers_collective_with_error(tmp_path):

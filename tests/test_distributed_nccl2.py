@@ -1,0 +1,102 @@
+"""DistributedOzakiCRT on two GPUs over NCCL (skipped when the machine has fewer than two): the pre-placed grid of C
+blocks, B broadcast from one rank inside the call, and A, B on one rank with scatter / broadcast / gather.  Every C
+must equal the single-GPU product bit for bit, and both ranks must decide the same (N, p).  The ranks are spawned
+child processes, one per GPU; the process group has a short timeout so that a failure ends the test instead of
+hanging it."""
+import os
+import socket
+import sys
+import traceback
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SHAPE = (512, 768, 384)                        # m, k, n
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, outdir):
+    try:
+        sys.path.insert(0, ROOT)
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        import __graft_entry__
+        pkg = __graft_entry__.load_package()
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        from matrix_numbers_b200.distributed import DistributedOzakiCRT
+        m, k, n = SHAPE
+        A, B = pkg.make_inputs(m, k, n, 2.0, seed=44)
+        rows = m // world
+        A_rows = torch.from_numpy(np.ascontiguousarray(A[rank * rows:(rank + 1) * rows])).to(dev)
+        B_full = torch.from_numpy(B).to(dev)
+        D = DistributedOzakiCRT(grid=(world, 1))
+        out = {}
+        C, info = D.run(A_rows, B_full)
+        out["pre"] = (C.cpu().numpy(), (info["N"], info["p"], info["preq"]))
+        root = world - 1
+        C, info = D.run_broadcast_b(A_rows, B_full if rank == root else None, root=root)
+        out["bcast"] = (C.cpu().numpy(), (info["N"], info["p"], info["preq"]))
+        A_full = torch.from_numpy(A).to(dev)
+        C, info = D.run_from_root(A_full if rank == root else None, B_full if rank == root else None, root=root)
+        out["root"] = (C.cpu().numpy(), (info["N"], info["p"], info["preq"]))
+        torch.cuda.synchronize()
+        D.engine.check_errors()
+        for name, (Cn, dec) in out.items():
+            np.save(os.path.join(outdir, f"{name}_{rank}.npy"), Cn)
+            with open(os.path.join(outdir, f"{name}_{rank}.txt"), "w") as f:
+                f.write(repr(dec))
+        if rank == 0:
+            E = pkg.OzakiCRT()
+            Cs, i_s = E.run(A_full, B_full)
+            np.save(os.path.join(outdir, "single.npy"), Cs.cpu().numpy())
+            with open(os.path.join(outdir, "single.txt"), "w") as f:
+                f.write(repr((i_s["N"], i_s["p"], i_s["p_req"])))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        with open(os.path.join(outdir, f"error_{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+
+
+def test_two_ranks_nccl_bit_exact(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(timeout=240)
+    alive = [p.is_alive() for p in ctx.processes]
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    assert not any(alive), "a rank did not finish"
+    errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    single = np.load(os.path.join(tmp_path, "single.npy")).view(np.uint64)
+    want = eval(open(os.path.join(tmp_path, "single.txt")).read())
+    for name in ("pre", "bcast"):
+        C = np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{r}.npy")) for r in range(world)])
+        np.testing.assert_array_equal(C.view(np.uint64), single, err_msg=name)
+    np.testing.assert_array_equal(np.load(os.path.join(tmp_path, f"root_{world - 1}.npy")).view(np.uint64), single)
+    for name in ("pre", "bcast", "root"):
+        for r in range(world):
+            assert eval(open(os.path.join(tmp_path, f"{name}_{r}.txt")).read()) == want, (name, r)

@@ -544,3 +544,34 @@ def test_rule_hard_selection(pkg, oracle, torch_mod, m, n, ties):
     I = raw[168:168 + 96 * 4].view(np.int32)[:min(32, m)]
     J = raw[552:552 + 96 * 4].view(np.int32)[:min(32, n)]
     assert np.array_equal(I, oracle.hard_top(r, sA, k)) and np.array_equal(J, oracle.hard_top(c, sB, k))
+
+
+@pytest.mark.parametrize("shape,phi,seed", [((256, 1024, 192), 1.0, 21), ((384, 640, 96), 2.0, 22)])
+def test_ozk_core_c_abi_equals_engine_core(pkg, oracle, engine, torch_mod, shape, phi, seed):
+    """``ozk_core``, the one-call replacement of the reference's core() (ozaki_engine.py:1310-1350) that an
+    integrator binds directly, called through ctypes with its own plane buffers: C bit for bit equal to
+    ``engine.core`` and to the oracle, with skip_a reusing the A planes of the first call."""
+    torch = torch_mod
+    L, ptr = pkg._lib.lib(), pkg._lib.ptr
+    m, k, n = shape
+    A, B = pkg.make_inputs(m, k, n, phi, seed)
+    Ad, Bd = T(torch, A), T(torch, B)
+    C_ref, info = engine.run(Ad, Bd)
+    N, p = info["N"], info["p"]
+    b = engine.buffers(m, n, k, N)
+    engine.stats(Ad, Bd, b, True)
+    b["pdev"].fill_(p)
+    Ares = torch.empty(N * m * k, dtype=torch.int8, device="cuda")
+    Bres = torch.empty(N * n * k, dtype=torch.int8, device="cuda")
+    X = torch.empty(N * m * n, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for skip_a in (0, 1):
+        C = torch.full((m, n), float("nan"), dtype=torch.float64, device="cuda")
+        pkg._lib.check(L.ozk_core(ptr(Ad), ptr(Bd), ptr(b["gam"]), ptr(b["r"]), ptr(b["c"]), ptr(b["pdev"]), m, n, k,
+                                  N, skip_a, ptr(Ares), ptr(Bres), ptr(X), ptr(C), ptr(err), st), "ozk_core")
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert torch.equal(C, C_ref), skip_a
+    st_o = oracle.stats(A, B, True)
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint64), oracle.core(A, B, st_o, N, p).view(np.uint64))

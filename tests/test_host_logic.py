@@ -111,3 +111,18 @@ def test_oracle_probe_sets_follow_reference(oracle):
     assert np.array_equal(Jr, rs.choice(200, 64, replace=False))
     Ir, Jr = oracle.probe_random(40, 32, seed=1)
     assert len(Ir) == 40 and len(Jr) == 32
+
+
+def test_correctly_rounded_products_are_exact(pkg):
+    """The accuracy sample's reference values (Dekker products + fsum) equal the exact rational dot product rounded
+    once, including a cancelling case."""
+    from fractions import Fraction
+    A, B = pkg.make_inputs(6, 200, 5, 2.0, seed=13)
+    B[:, 4] = A[0] * 3.0                       # column 4: row 0's dot product has no cancellation...
+    A[1] = -A[0]                               # ...and row 1's is its exact negative
+    got = pkg.correctly_rounded_products(A, B)
+    for i in range(A.shape[0]):
+        for j in range(B.shape[1]):
+            exact = sum(Fraction(float(a)) * Fraction(float(b)) for a, b in zip(A[i], B[:, j]))
+            assert got[i, j] == float(exact), (i, j)
+    assert got[1, 4] == -got[0, 4]
