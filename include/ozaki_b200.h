@@ -45,6 +45,7 @@ typedef void* ozk_stream_t;
 #define OZK_DEVERR_TIMEOUT_PRODUCER 1   /* GEMM: the TMA producer's bounded wait ran out   */
 #define OZK_DEVERR_TIMEOUT_MMA 2        /* GEMM: the MMA issuer's bounded wait ran out     */
 #define OZK_DEVERR_TIMEOUT_EPILOGUE 4   /* GEMM: an epilogue warp's bounded wait ran out   */
+#define OZK_DEVERR_TIMEOUT_RECON 8      /* reconstruction: a bounded wait (TMA or MMA) ran out */
 
 /* ---- library information -------------------------------------------------------------------------------- */
 int ozk_version(void);
@@ -179,9 +180,11 @@ int ozk_wait_selftest(int role, int64_t limit_ns, int32_t* err, int64_t* waited_
 
 /* ---- stage 3c: CRT reconstruction and unscale (replaces recon_k, ozaki_engine.py:1040-1101) ------------- *
  * C[i][j] = the correctly rounded double of the symmetric CRT lift of X[.][i][j], times 2^(r_i + c_j - 2p)
- * (the ldexp rounding of the reference in the subnormal range).                                            */
+ * (the ldexp rounding of the reference in the subnormal range).  The CRT sums run on the tensor cores
+ * (tcgen05.mma kind::i8 over TMA tiles of X); err: device int32, OZK_DEVERR_TIMEOUT_RECON is OR'ed in if one of
+ * the kernel's bounded waits runs out (C is then invalid).                                                    */
 int ozk_reconstruct(const uint8_t* X, const int32_t* r, const int32_t* c, const int32_t* p_dev, int m, int n, int N,
-                    double* C, ozk_stream_t stream);
+                    double* C, int32_t* err, ozk_stream_t stream);
 
 /* ---- residue chains (the chain cost law of code/digit_gemm.py:1252-1291, executed): the product planes of
  * ozk_gemm_residues, X[t] in [0, m_t), mapped to the symmetric int8 residues of the split,

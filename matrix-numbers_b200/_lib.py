@@ -55,7 +55,7 @@ _SIGNATURES = {
     "ozk_gemm_residues": ([P, P, I32, I32, I32, I32, P, P, P], I32),
     "ozk_gemm_i32": ([P, P, I32, I32, I32, P, P, P], I32),
     "ozk_wait_selftest": ([I32, ctypes.c_int64, P, P, P], I32),
-    "ozk_reconstruct": ([P, P, P, P, I32, I32, I32, P, P], I32),
+    "ozk_reconstruct": ([P, P, P, P, I32, I32, I32, P, P, P], I32),
     "ozk_core": ([P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P], I32),
 }
 

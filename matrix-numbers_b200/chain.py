@@ -121,7 +121,7 @@ class ResidueChain:
             del right
         n = mats[-1].shape[1]
         C = torch.empty((m, n), dtype=torch.float64, device=dev)
-        check(self.lib.ozk_reconstruct(ptr(X), ptr(rows), ptr(cols), ptr(pdev), m, n, N, ptr(C), st),
+        check(self.lib.ozk_reconstruct(ptr(X), ptr(rows), ptr(cols), ptr(pdev), m, n, N, ptr(C), ptr(err), st),
               "ozk_reconstruct")
         self.launches += 1
         if int(err.item()):

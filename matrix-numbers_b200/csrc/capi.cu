@@ -113,5 +113,5 @@ extern "C" int ozk_core(const double* A, const double* B, const int32_t* gam, co
     if (!skip_a && (rc = ozk_split_a(A, r, gam, p_dev, m, k, N, Ares, stream)) != OZK_OK) return rc;
     if ((rc = ozk_split_b(B, c, gam, p_dev, k, n, N, Bres, stream)) != OZK_OK) return rc;
     if ((rc = ozk_gemm_residues(Ares, Bres, m, n, k, N, X, err, stream)) != OZK_OK) return rc;
-    return ozk_reconstruct(X, r, c, p_dev, m, n, N, C, stream);
+    return ozk_reconstruct(X, r, c, p_dev, m, n, N, C, err, stream);
 }

@@ -184,8 +184,8 @@ class Workspace:
     @staticmethod
     def raise_on_device_error(word: int):
         if word:
-            raise _lib.OzkError(f"device error flag {word:#x} raised by an INT8 GEMM launch (a bounded wait ran out); "
-                                "the results of that call are invalid")
+            raise _lib.OzkError(f"device error flag {word:#x} raised by a product or reconstruction launch (a bounded "
+                                "wait ran out); the results of that call are invalid")
 
     def host_stats(self):
         """(statistics dict of numpy arrays, non-finite flag) read from the device (synchronises)."""
@@ -393,7 +393,7 @@ class OzakiCRT:
                                          ptr(b.error_word), st), "ozk_gemm_residues")
         mark("gemm+reduce")
         check(self.lib.ozk_reconstruct(ptr(b.planes_X), ptr(r_rows), ptr(b.c), ptr(b.p_core), rows, n, N, ptr(C_rows),
-                                       st), "ozk_reconstruct")
+                                       ptr(b.error_word), st), "ozk_reconstruct")
         mark("recon")
         self.launches += launched + 2
 

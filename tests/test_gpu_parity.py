@@ -367,8 +367,11 @@ def test_reconstruct_random_residues(pkg, oracle, torch_mod, N, n):
         Xd, rd, cd = T(torch, X), T(torch, r), T(torch, c)
         pd = torch.tensor([p], dtype=torch.int32, device="cuda")
         C = torch.empty((m, n), dtype=torch.float64, device="cuda")
-        pkg._lib.check(L.ozk_reconstruct(ptr(Xd), ptr(rd), ptr(cd), ptr(pd), m, n, N, ptr(C), torch.cuda.current_stream().cuda_stream), "recon")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        pkg._lib.check(L.ozk_reconstruct(ptr(Xd), ptr(rd), ptr(cd), ptr(pd), m, n, N, ptr(C), ptr(err),
+                                         torch.cuda.current_stream().cuda_stream), "recon")
         torch.cuda.synchronize()
+        assert int(err.item()) == 0
         want = oracle.recon(X, r, c, p)
         np.testing.assert_array_equal(C.cpu().numpy().view(np.uint64), want.view(np.uint64))
 
@@ -390,8 +393,11 @@ def test_reconstruct_extreme_exponents(pkg, oracle, torch_mod):
         Xd, rd, cd = T(torch, X), T(torch, r), T(torch, c)
         pd = torch.tensor([p], dtype=torch.int32, device="cuda")
         C = torch.empty((m, n), dtype=torch.float64, device="cuda")
-        pkg._lib.check(L.ozk_reconstruct(ptr(Xd), ptr(rd), ptr(cd), ptr(pd), m, n, N, ptr(C), torch.cuda.current_stream().cuda_stream), "recon")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        pkg._lib.check(L.ozk_reconstruct(ptr(Xd), ptr(rd), ptr(cd), ptr(pd), m, n, N, ptr(C), ptr(err),
+                                         torch.cuda.current_stream().cuda_stream), "recon")
         torch.cuda.synchronize()
+        assert int(err.item()) == 0
         np.testing.assert_array_equal(C.cpu().numpy().view(np.uint64), oracle.recon(X, r, c, p).view(np.uint64))
 
 

@@ -93,7 +93,7 @@ def test_capi_host_calls_without_device(pkg):
     # argument validation happens before any device work: null pointers are rejected with OZK_ERR_ARG
     assert lib.ozk_split_a(None, None, None, None, 4, 32, 16, None, None) == -1
     assert lib.ozk_gemm_residues(None, None, 4, 32, 32, 16, None, None, None) == -1
-    assert lib.ozk_reconstruct(None, None, None, None, 4, 32, 16, None, None) == -1
+    assert lib.ozk_reconstruct(None, None, None, None, 4, 32, 16, None, None, None) == -1
     assert lib.ozk_wait_selftest(0, 10**6, None, None, None) == -1
     assert lib.ozk_wait_selftest(2, 10**6, 16, 16, None) == -1           # role outside {0, 1}
     assert lib.ozk_wait_selftest(0, 999, 16, 16, None) == -1             # limit below 1 us
