@@ -66,6 +66,45 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int32_t* e
     atomicOr(err, code);
 }
 
+// One thread's 32 consecutive accumulator columns of a row: stored as INT32 (MODE_I32) or reduced modulo m_t to a
+// residue byte, added modulo m_t to the residues of earlier k segments (seg > 0)
+template <int MODE>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int row, int col, int t, int seg, int m, int n,
+                                               const ModParams& mp, void* __restrict__ out) {
+    if (MODE == MODE_I32) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<int32_t*>(out) + (size_t)row * n + col);
+#pragma unroll
+        for (int q = 0; q < 8; q++) dst[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+        const uint32_t P = mp.P[t], R = mp.R16[t], MG = mp.MG[t], OFF = mp.OFF[t];
+        uint32_t rs[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+            const uint32_t uu = v[e] + OFF;
+            const uint32_t s = (uu >> 16) * R + (uu & 0xffffu);
+            rs[e] = s - __umulhi(s, MG) * P;
+        }
+        uint8_t* xrow = static_cast<uint8_t*>(out) + ((size_t)t * m + row) * (size_t)n + col;
+        uint4* dst = reinterpret_cast<uint4*>(xrow);
+        if (seg > 0) {
+            // add this segment's residues to the ones stored by this thread for earlier segments
+            const uint4 p0 = dst[0], p1 = dst[1];
+            const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                uint32_t a = rs[e] + ((pw[e >> 2] >> (8 * (e & 3))) & 0xffu);
+                rs[e] = a >= P ? a - P : a;
+            }
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+            w[q] = rs[4 * q] | (rs[4 * q + 1] << 8) | (rs[4 * q + 2] << 16) | (rs[4 * q + 3] << 24);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ out,
@@ -221,40 +260,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN + col_local), v);
                     tmem_wait_ld();
                     const int col = tn * BN + col_local;
-                    if (row < m && col < n) {
-                        if (MODE == MODE_I32) {
-                            uint4* dst = reinterpret_cast<uint4*>(static_cast<int32_t*>(out) + (size_t)row * n + col);
-#pragma unroll
-                            for (int q = 0; q < 8; q++) dst[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                        } else {
-                            const uint32_t P = mp.P[t], R = mp.R16[t], MG = mp.MG[t], OFF = mp.OFF[t];
-                            uint32_t rs[32];
-#pragma unroll
-                            for (int e = 0; e < 32; e++) {
-                                const uint32_t uu = v[e] + OFF;
-                                const uint32_t s = (uu >> 16) * R + (uu & 0xffffu);
-                                rs[e] = s - __umulhi(s, MG) * P;
-                            }
-                            uint8_t* xrow = static_cast<uint8_t*>(out) + ((size_t)t * m + row) * (size_t)n + col;
-                            uint4* dst = reinterpret_cast<uint4*>(xrow);
-                            if (seg > 0) {
-                                // add this segment's residues to the ones stored by this thread for earlier segments
-                                const uint4 p0 = dst[0], p1 = dst[1];
-                                const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-#pragma unroll
-                                for (int e = 0; e < 32; e++) {
-                                    uint32_t a = rs[e] + ((pw[e >> 2] >> (8 * (e & 3))) & 0xffu);
-                                    rs[e] = a >= P ? a - P : a;
-                                }
-                            }
-                            uint32_t w[8];
-#pragma unroll
-                            for (int q = 0; q < 8; q++)
-                                w[q] = rs[4 * q] | (rs[4 * q + 1] << 8) | (rs[4 * q + 2] << 16) | (rs[4 * q + 3] << 24);
-                            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                        }
-                    }
+                    if (row < m && col < n) epilogue_chunk<MODE>(v, row, col, t, seg, m, n, mp, out);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -270,6 +276,222 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) {
         __syncwarp();
         tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---- the two-SM tile (tcgen05 cta_group::2) -------------------------------------------------------------------
+// A cluster of two CTAs on a pair of SMs computes a 256 x 256 tile of one modulus: CTA r holds rows 128 r .. 128 r +
+// 127 of the A tile and columns 128 r .. 128 r + 127 of the B tile (K-major, 128-byte swizzle, at the same shared
+// memory offsets in both CTAs), so each SM streams 32 KB per 128-deep k block instead of 48 KB, and six stages fit.
+//   - both CTAs' warp 0 load their halves with TMA; every load completes on CTA 0's full barrier, which CTA 0's
+//     producer arms with the bytes of both halves (no multicast: each CTA loads only its own data);
+//   - CTA 0's warp 1 issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32): it reads A and B from both CTAs'
+//     shared memory and writes each CTA's TMEM with its own 128 rows; its commits arrive on the stage's empty barrier
+//     and on the accumulator-full barrier of both CTAs (one commit per barrier);
+//   - the epilogue warps of both CTAs drain their own TMEM as in the one-SM kernel and arrive on CTA 0's
+//     accumulator-empty barrier (the follower's arrivals are remote, at cluster scope);
+//   - the CTAs meet at a cluster barrier after initialisation and before TMEM is freed, so no CTA leaves while its
+//     peer can still write its TMEM or its barriers; every other wait is bounded, as in the one-SM kernel.
+constexpr int HALF = 128;                    // rows of A and of B held by each CTA of the pair
+constexpr int BM2 = 2 * HALF, BN2 = 2 * HALF;
+constexpr int STAGES2 = 6;
+constexpr uint32_t A2_BYTES = HALF * BK, B2_BYTES = HALF * BK;
+constexpr uint32_t STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr int GROUP_M2 = 8;                  // 8 tile-rows of 256 = the 16 tile-rows of 128 of the one-SM kernel
+constexpr uint32_t IDESC2 = umma_idesc_i8(BM2, BN2);
+constexpr int NUM_BARS2 = 2 * STAGES2 + 5;   // full[S], empty[S], acc_full[2], acc_empty[2], drain
+constexpr size_t SMEM2_BYTES = (size_t)STAGES2 * STAGE2_BYTES + 1024 + 256;
+static_assert(NUM_BARS2 * 8 + 16 <= 256, "barrier area");
+static_assert(BN2 == BN, "the epilogue covers the 256 accumulator columns of the one-SM kernel");
+
+__device__ __forceinline__ void decode_unit2(int u, int tiles, int tiles_m, int tiles_n, int& t, int& tm, int& tn) {
+    t = u / tiles;
+    const int tile = u - t * tiles;
+    const int per_group = GROUP_M2 * tiles_n;
+    const int g = tile / per_group;
+    const int first_m = g * GROUP_M2;
+    const int gm = min(tiles_m - first_m, GROUP_M2);
+    const int in = tile - g * per_group;
+    tm = first_m + in % gm;
+    tn = in / gm;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    void* __restrict__ out, int m, int n, int k, int N, const __grid_constant__ ModParams mp,
+                    int32_t* __restrict__ err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES2 * A2_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();           // 0: issues the MMAs; 1: its peer
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * (uint32_t)s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (uint32_t)(STAGES2 + s); };
+    auto accf_bar = [&](int b) { return bar0 + 8u * (uint32_t)(2 * STAGES2 + b); };
+    auto acce_bar = [&](int b) { return bar0 + 8u * (uint32_t)(2 * STAGES2 + 2 + b); };
+    const uint32_t drain_bar = bar0 + 8u * (uint32_t)(2 * STAGES2 + 4);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES2; s++) { mbar_init(full_bar(s), 1); mbar_init(empty_bar(s), 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(accf_bar(b), 1); mbar_init(acce_bar(b), 2 * EPI_WARPS); }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                                    // the peer's barriers exist before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int tiles_m = (m + BM2 - 1) / BM2, tiles_n = (n + BN2 - 1) / BN2;
+    const int tiles = tiles_m * tiles_n;
+    const int units = N * tiles;
+    const int kblocks = (k + BK - 1) / BK;
+    const int nseg = (kblocks + SEG_KB - 1) / SEG_KB;
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer (both CTAs)
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int u = pair; ok && u < units; u += npairs) {
+                int t, tm, tn;
+                decode_unit2(u, tiles, tiles_m, tiles_n, t, tm, tn);
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_LIMIT_NS)) {
+                        if (!*abort_flag) raise_abort(abort_flag, err, OZK_DEVERR_TIMEOUT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full0 = map_to_rank(full_bar(stage), 0u);
+                    if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2u * STAGE2_BYTES);
+                    tma_load_3d_pair(smem_addr(sA + stage * A2_BYTES), &tmA, kb * BK, tm * BM2 + (int)rank * HALF, t,
+                                     full0);
+                    tma_load_3d_pair(smem_addr(sB + stage * B2_BYTES), &tmB, kb * BK, tn * BN2 + (int)rank * HALF, t,
+                                     full0);
+                    issued++;
+                    if (++stage == STAGES2) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok && rank == 0) {
+                // let the loads already armed land before the pair exits (bounded)
+                const long long first = issued > STAGES2 ? issued - STAGES2 : 0;
+                for (long long j = first; j < issued; j++) {
+                    const int s = (int)(j % STAGES2);
+                    const uint32_t par = (uint32_t)((j / STAGES2) & 1);
+                    int dummy = 0;
+                    mbar_wait_bounded(full_bar(s), par, &dummy, WAIT_LIMIT_NS);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ------------------------------------------------------------ MMA issuer (CTA 0 of the pair)
+            int stage = 0;
+            uint32_t phase = 0, acc_it = 0;
+            bool ok = true, issued_any = false;
+            for (int u = pair; ok && u < units; u += npairs) {
+                for (int seg = 0; ok && seg < nseg; seg++) {
+                    const int b = (int)(acc_it & 1u);
+                    const uint32_t aph = (acc_it >> 1) & 1u;
+                    if (!mbar_wait_bounded(acce_bar(b), aph ^ 1u, abort_flag, WAIT_LIMIT_NS)) {
+                        if (!*abort_flag) raise_abort(abort_flag, err, OZK_DEVERR_TIMEOUT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN2);
+                    const int kb0 = seg * SEG_KB, kb1 = min(kblocks, kb0 + SEG_KB);
+                    for (int kb = kb0; kb < kb1; kb++) {
+                        if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, WAIT_LIMIT_NS)) {
+                            if (!*abort_flag) raise_abort(abort_flag, err, OZK_DEVERR_TIMEOUT_MMA);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t adesc = umma_desc_sw128(smem_addr(sA + stage * A2_BYTES));
+                        const uint64_t bdesc = umma_desc_sw128(smem_addr(sB + stage * B2_BYTES));
+#pragma unroll
+                        for (int kk = 0; kk < BK / 32; kk++)
+                            umma_i8_pair(d_tmem, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), IDESC2,
+                                         (kb > kb0 || kk > 0) ? 1u : 0u);
+                        issued_any = true;
+                        umma_commit_pair(empty_bar(stage));
+                        umma_commit_pair(map_to_rank(empty_bar(stage), 1u));
+                        if (++stage == STAGES2) { stage = 0; phase ^= 1u; }
+                    }
+                    if (!ok) break;
+                    umma_commit_pair(accf_bar(b));
+                    umma_commit_pair(map_to_rank(accf_bar(b), 1u));
+                    acc_it++;
+                }
+            }
+            if (!ok && issued_any) {
+                // every MMA issued by this thread finishes before the pair's TMEM is released
+                umma_commit_pair(drain_bar);
+                int dummy = 0;
+                mbar_wait_bounded(drain_bar, 0u, &dummy, WAIT_LIMIT_NS);
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue warps (both CTAs)
+        const int ew = warp - 2;
+        const int quarter = warp & 3;          // TMEM lanes this warp may access: [32 quarter, 32 quarter + 32)
+        const int half = ew >> 2;              // column half of the 256-column accumulator
+        uint32_t acc_it = 0;
+        bool ok = true;
+        for (int u = pair; ok && u < units; u += npairs) {
+            int t, tm, tn;
+            decode_unit2(u, tiles, tiles_m, tiles_n, t, tm, tn);
+            const int row = tm * BM2 + (int)rank * HALF + quarter * 32 + lane;
+            for (int seg = 0; seg < nseg; seg++) {
+                const int b = (int)(acc_it & 1u);
+                const uint32_t aph = (acc_it >> 1) & 1u;
+                bool w = mbar_wait_bounded(accf_bar(b), aph, abort_flag, WAIT_LIMIT_NS);
+                if (!w && !*abort_flag) raise_abort(abort_flag, err, OZK_DEVERR_TIMEOUT_EPILOGUE);
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll 1
+                for (int cc = 0; cc < 4; cc++) {
+                    const int col_local = half * 128 + cc * 32;
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN2 + col_local), v);
+                    tmem_wait_ld();
+                    const int col = tn * BN2 + col_local;
+                    if (row < m && col < n) epilogue_chunk<MODE>(v, row, col, t, seg, m, n, mp, out);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(map_to_rank(acce_bar(b), 0u));
+                acc_it++;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                                    // neither CTA leaves while its peer may still reach it
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -363,7 +585,12 @@ ModParams make_mod_params() {
     return mp;
 }
 
-struct DeviceInfo { int sms = 0; bool attr_res = false, attr_i32 = false; };
+struct DeviceInfo {
+    int sms = 0;
+    bool attr_res = false, attr_i32 = false;
+    bool attr2_res = false, attr2_i32 = false;
+    int pairs = 0;                           // CTA pairs of the two-SM kernel that fit on the device at once
+};
 DeviceInfo g_dev[64];
 
 int device_info(DeviceInfo** out) {
@@ -406,6 +633,52 @@ int launch_gemm(const int8_t* Ares, const int8_t* Bres, int m, int n, int k, int
     return OZK_OK;
 }
 
+// The two-SM kernel: one cluster of two CTAs per pair of SMs, persistent over 256 x 256 tiles
+template <int MODE>
+int launch_gemm2(const int8_t* Ares, const int8_t* Bres, int m, int n, int k, int N, void* out, int32_t* err,
+                 cudaStream_t st) {
+    DeviceInfo* d = nullptr;
+    int rc = device_info(&d);
+    if (rc != OZK_OK) return rc;
+    bool& attr = MODE == MODE_I32 ? d->attr2_i32 : d->attr2_res;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute cluster[1];
+    cluster[0].id = cudaLaunchAttributeClusterDimension;
+    cluster[0].val.clusterDim.x = 2;
+    cluster[0].val.clusterDim.y = 1;
+    cluster[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    cfg.stream = st;
+    cfg.attrs = cluster;
+    cfg.numAttrs = 1;
+    if (!attr) {
+        if (cudaFuncSetAttribute(gemm_tc2_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SMEM2_BYTES) != cudaSuccess)
+            return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
+        if (d->pairs == 0) {
+            cfg.gridDim = dim3(2 * (d->sms / 2), 1, 1);
+            int pairs = 0;
+            if (cudaOccupancyMaxActiveClusters(&pairs, gemm_tc2_kernel<MODE>, &cfg) != cudaSuccess || pairs < 1)
+                return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
+            d->pairs = pairs;
+        }
+        attr = true;
+    }
+    CUtensorMap ta, tb;
+    if ((rc = make_plane_map(&ta, Ares, k, m, N, HALF)) != OZK_OK) return rc;
+    if ((rc = make_plane_map(&tb, Bres, k, n, N, HALF)) != OZK_OK) return rc;
+    const long long units = (long long)N * ((m + BM2 - 1) / BM2) * ((n + BN2 - 1) / BN2);
+    if (units > 0x7fffffffLL) return OZK_ERR_ARG;
+    const int pairs = (int)(units < d->pairs ? units : d->pairs);
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    static const ModParams mp = make_mod_params();
+    if (cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<MODE>, ta, tb, out, m, n, k, N, mp, err) != cudaSuccess)
+        return OZK_ERR_CUDA_BASE + (int)cudaGetLastError();
+    OZK_CHECK_LAUNCH();
+    return OZK_OK;
+}
+
 bool shapes_ok(const void* a, const void* b, const void* out, const void* err, int m, int n, int k) {
     if (!a || !b || !out || !err) return false;
     if (m <= 0 || n <= 0 || k <= 0 || (m & 3) || (n & 31) || (k & 31)) return false;
@@ -419,13 +692,17 @@ bool shapes_ok(const void* a, const void* b, const void* out, const void* err, i
 extern "C" int ozk_gemm_residues(const int8_t* Ares, const int8_t* Bres, int m, int n, int k, int N, uint8_t* X,
                                  int32_t* err, ozk_stream_t stream) {
     if (!shapes_ok(Ares, Bres, X, err, m, n, k) || N < 1 || N > OZK_NMAX) return OZK_ERR_ARG;
-    return launch_gemm<MODE_RESIDUE>(Ares, Bres, m, n, k, N, X, err, reinterpret_cast<cudaStream_t>(stream));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (m > HALF) return launch_gemm2<MODE_RESIDUE>(Ares, Bres, m, n, k, N, X, err, st);
+    return launch_gemm<MODE_RESIDUE>(Ares, Bres, m, n, k, N, X, err, st);
 }
 
 extern "C" int ozk_gemm_i32(const int8_t* A_plane, const int8_t* B_plane, int m, int n, int k, int32_t* C32,
                             int32_t* err, ozk_stream_t stream) {
     if (!shapes_ok(A_plane, B_plane, C32, err, m, n, k) || k > OZK_KSEG) return OZK_ERR_ARG;
-    return launch_gemm<MODE_I32>(A_plane, B_plane, m, n, k, 1, C32, err, reinterpret_cast<cudaStream_t>(stream));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (m > HALF) return launch_gemm2<MODE_I32>(A_plane, B_plane, m, n, k, 1, C32, err, st);
+    return launch_gemm<MODE_I32>(A_plane, B_plane, m, n, k, 1, C32, err, st);
 }
 
 extern "C" int ozk_wait_selftest(int role, int64_t limit_ns, int32_t* err, int64_t* waited_ns, ozk_stream_t stream) {

@@ -312,7 +312,8 @@ def test_gemm_i32_exact(pkg, oracle, torch_mod, m, n, k):
         assert torch.equal(C, ref)
 
 
-@pytest.mark.parametrize("m,n,k,N", [(256, 256, 256, 20), (132, 160, 288, 32), (512, 768, 640, 16), (8, 64, 64, 6)])
+@pytest.mark.parametrize("m,n,k,N", [(256, 256, 256, 20), (132, 160, 288, 32), (512, 768, 640, 16), (8, 64, 64, 6),
+                                     (640, 1280, 512, 18), (1152, 256, 384, 3)])
 def test_gemm_residues_exact(pkg, oracle, torch_mod, m, n, k, N):
     torch = torch_mod
     rng = np.random.default_rng(m + 3 * n + 5 * k + N)
