@@ -679,6 +679,11 @@ int launch_gemm2(const int8_t* Ares, const int8_t* Bres, int m, int n, int k, in
     return OZK_OK;
 }
 
+// Which tile: the two-SM kernel reads half the operand bytes per SM and is faster where a plane's operands stay in
+// L2 (c2 +2 %, c5 (2048 x 2048, k = 262144) +14 % on one B200); on larger planes that stream from DRAM the one-SM
+// kernel was faster under the 1 kW power cap (c3 -12 %, c4 -30 % for the two-SM kernel, same GPU, alternating runs)
+bool use_pair_tiles(int m, int n) { return m > HALF && (long long)m * n <= 4096LL * 4096LL; }
+
 bool shapes_ok(const void* a, const void* b, const void* out, const void* err, int m, int n, int k) {
     if (!a || !b || !out || !err) return false;
     if (m <= 0 || n <= 0 || k <= 0 || (m & 3) || (n & 31) || (k & 31)) return false;
@@ -693,7 +698,7 @@ extern "C" int ozk_gemm_residues(const int8_t* Ares, const int8_t* Bres, int m, 
                                  int32_t* err, ozk_stream_t stream) {
     if (!shapes_ok(Ares, Bres, X, err, m, n, k) || N < 1 || N > OZK_NMAX) return OZK_ERR_ARG;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (m > HALF) return launch_gemm2<MODE_RESIDUE>(Ares, Bres, m, n, k, N, X, err, st);
+    if (use_pair_tiles(m, n)) return launch_gemm2<MODE_RESIDUE>(Ares, Bres, m, n, k, N, X, err, st);
     return launch_gemm<MODE_RESIDUE>(Ares, Bres, m, n, k, N, X, err, st);
 }
 
@@ -701,7 +706,7 @@ extern "C" int ozk_gemm_i32(const int8_t* A_plane, const int8_t* B_plane, int m,
                             int32_t* err, ozk_stream_t stream) {
     if (!shapes_ok(A_plane, B_plane, C32, err, m, n, k) || k > OZK_KSEG) return OZK_ERR_ARG;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (m > HALF) return launch_gemm2<MODE_I32>(A_plane, B_plane, m, n, k, 1, C32, err, st);
+    if (use_pair_tiles(m, n)) return launch_gemm2<MODE_I32>(A_plane, B_plane, m, n, k, 1, C32, err, st);
     return launch_gemm<MODE_I32>(A_plane, B_plane, m, n, k, 1, C32, err, st);
 }
 
