@@ -46,6 +46,7 @@ typedef void* ozk_stream_t;
 #define OZK_DEVERR_TIMEOUT_MMA 2        /* GEMM: the MMA issuer's bounded wait ran out     */
 #define OZK_DEVERR_TIMEOUT_EPILOGUE 4   /* GEMM: an epilogue warp's bounded wait ran out   */
 #define OZK_DEVERR_TIMEOUT_RECON 8      /* reconstruction: a bounded wait (TMA or MMA) ran out */
+#define OZK_DEVERR_TIMEOUT_SPLIT 16     /* residue split: a bounded wait (TMA or MMA) ran out  */
 
 /* ---- library information -------------------------------------------------------------------------------- */
 int ozk_version(void);
@@ -157,9 +158,9 @@ int ozk_rule_finish(const int32_t* r, const int32_t* c, const double* sA, const 
  * Ares[t][i][l] = symmetric residue of round(A_il 2^(p - r_i + gam_l)) modulo m_t, t < N, as int8;
  * Bres[t][j][l] = the same for B_lj 2^(p - c_j - gam_l), contraction index contiguous (K-major planes).     */
 int ozk_split_a(const double* A, const int32_t* r, const int32_t* gam, const int32_t* p_dev, int m, int k, int N,
-                int8_t* Ares, ozk_stream_t stream);
+                int8_t* Ares, int32_t* err, ozk_stream_t stream);
 int ozk_split_b(const double* B, const int32_t* c, const int32_t* gam, const int32_t* p_dev, int k, int n, int N,
-                int8_t* Bres, ozk_stream_t stream);
+                int8_t* Bres, int32_t* err, ozk_stream_t stream);
 
 /* ---- stage 3b: the N INT8 products with the modular reduction fused into the epilogue (replaces the
  * cuBLASLt INT8 GEMM loop and reduce_k, ozaki_engine.py:1333-1341 and :952-967).  Persistent tcgen05.mma

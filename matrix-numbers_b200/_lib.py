@@ -50,8 +50,8 @@ _SIGNATURES = {
     "ozk_rule_finish": ([P, P, P, P, I32, I32, I32, F64, F64, P, P, P, P, SZ, P], I32),
     "ozk_rule": ([P, P, I32, I32, I32, P, P, P, P, P, P, P, P, I32, P, I32, F64, F64, I32, I32, P, P, P, P, SZ, P], I32),
     "ozk_residue_symmetric": ([P, I32, SZ, P, P], I32),
-    "ozk_split_a": ([P, P, P, P, I32, I32, I32, P, P], I32),
-    "ozk_split_b": ([P, P, P, P, I32, I32, I32, P, P], I32),
+    "ozk_split_a": ([P, P, P, P, I32, I32, I32, P, P, P], I32),
+    "ozk_split_b": ([P, P, P, P, I32, I32, I32, P, P, P], I32),
     "ozk_gemm_residues": ([P, P, I32, I32, I32, I32, P, P, P], I32),
     "ozk_gemm_i32": ([P, P, I32, I32, I32, P, P, P], I32),
     "ozk_wait_selftest": ([I32, ctypes.c_int64, P, P, P], I32),
@@ -96,3 +96,14 @@ def check(rc: int, what: str) -> None:
 
 def ptr(t) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr())
+
+
+def split_kernels(src, out, vectors: int, k: int, is_b: bool) -> int:
+    """Kernels one ozk_split_a / ozk_split_b call launches: 2 when the tensor-core split takes the shape (it and the
+    general kernel are both launched; each returns at once for the p it does not cover), else 1.  Mirrors the
+    shape test of ozk_split_tc_launch (csrc/split_tc.cu)."""
+    if os.environ.get("OZK_SPLIT_TC", "1").startswith("0"):
+        return 1
+    ok = (vectors * k < 2 ** 32 and k % 32 == 0 and src.data_ptr() % 16 == 0 and out.data_ptr() % 8 == 0
+          and (not is_b or vectors % 16 == 0))
+    return 2 if ok else 1

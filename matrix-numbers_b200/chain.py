@@ -101,19 +101,20 @@ class ResidueChain:
         err = torch.zeros(1, dtype=torch.int32, device=dev)
         k1 = mats[0].shape[1]
         left = torch.empty((N, m, k1), dtype=torch.int8, device=dev)
-        check(self.lib.ozk_split_a(ptr(mats[0]), ptr(rows), ptr(gam), ptr(pdev), m, k1, N, ptr(left), st),
+        check(self.lib.ozk_split_a(ptr(mats[0]), ptr(rows), ptr(gam), ptr(pdev), m, k1, N, ptr(left), ptr(err), st),
               "ozk_split_a")
-        self.launches += 1
+        self.launches += _lib.split_kernels(mats[0], left, m, k1, False)
         X = None
         for s in range(1, len(mats)):
             k, n = mats[s].shape
             right = torch.empty((N, n, k), dtype=torch.int8, device=dev)
-            check(self.lib.ozk_split_b(ptr(mats[s]), ptr(cols), ptr(gam), ptr(pdev), k, n, N, ptr(right), st),
+            check(self.lib.ozk_split_b(ptr(mats[s]), ptr(cols), ptr(gam), ptr(pdev), k, n, N, ptr(right), ptr(err),
+                                       st),
                   "ozk_split_b")
             X = torch.empty((N, m, n), dtype=torch.uint8, device=dev)
             check(self.lib.ozk_gemm_residues(ptr(left), ptr(right), m, n, k, N, ptr(X), ptr(err), st),
                   "ozk_gemm_residues")
-            self.launches += 2
+            self.launches += _lib.split_kernels(mats[s], right, n, k, True) + 1
             if s + 1 < len(mats):
                 left = torch.empty((N, m, n), dtype=torch.int8, device=dev)
                 check(self.lib.ozk_residue_symmetric(ptr(X), N, m * n, ptr(left), st), "ozk_residue_symmetric")

@@ -18,7 +18,7 @@ OUT_DIR = os.path.join(PKG, "lib")
 OBJ_DIR = os.path.join(ROOT, "_build", "ozaki_b200")
 LIB = os.path.join(OUT_DIR, "libozaki_b200.so")
 
-SOURCES = ["capi.cu", "stats.cu", "rule.cu", "split.cu", "gemm_tc.cu", "recon.cu", "certificate.cu", "chain.cu"]
+SOURCES = ["capi.cu", "stats.cu", "rule.cu", "split.cu", "split_tc.cu", "gemm_tc.cu", "recon.cu", "certificate.cu", "chain.cu"]
 HEADERS = ["ozk_common.cuh", "tc_ptx.cuh"]
 
 

@@ -110,8 +110,8 @@ extern "C" int ozk_core(const double* A, const double* B, const int32_t* gam, co
                         const int32_t* p_dev, int m, int n, int k, int N, int skip_a, int8_t* Ares, int8_t* Bres,
                         uint8_t* X, double* C, int32_t* err, ozk_stream_t stream) {
     int rc;
-    if (!skip_a && (rc = ozk_split_a(A, r, gam, p_dev, m, k, N, Ares, stream)) != OZK_OK) return rc;
-    if ((rc = ozk_split_b(B, c, gam, p_dev, k, n, N, Bres, stream)) != OZK_OK) return rc;
+    if (!skip_a && (rc = ozk_split_a(A, r, gam, p_dev, m, k, N, Ares, err, stream)) != OZK_OK) return rc;
+    if ((rc = ozk_split_b(B, c, gam, p_dev, k, n, N, Bres, err, stream)) != OZK_OK) return rc;
     if ((rc = ozk_gemm_residues(Ares, Bres, m, n, k, N, X, err, stream)) != OZK_OK) return rc;
     return ozk_reconstruct(X, r, c, p_dev, m, n, N, C, err, stream);
 }

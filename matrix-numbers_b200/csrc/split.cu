@@ -403,9 +403,10 @@ __global__ void __launch_bounds__(kWarps * 32, OZK_SPLIT_MINB) split_kernel(cons
                                                                const int32_t* __restrict__ vexp,
                                                                const int32_t* __restrict__ gam,
                                                                const int32_t* __restrict__ p_dev, int V, int k, int N,
-                                                               int8_t* __restrict__ out) {
+                                                               int8_t* __restrict__ out, int p_lo) {
     __shared__ __align__(16) unsigned char strings[kWarps][kWarpSmem];
     const int p = *p_dev;
+    if (p < p_lo) return;   // split_tc.cu's kernel has produced the planes
     unsigned char* wsm = strings[threadIdx.x >> 5];
     if (p <= 119) split_tasks<16, IS_B, PACKED>(src, vexp, gam, p, V, k, N, out, wsm);
     else split_tasks<32, IS_B, false>(src, vexp, gam, p, V, k, N, out, wsm);
@@ -421,34 +422,46 @@ int split_blocks(long long tasks) {
 
 }  // namespace
 
+// split_tc.cu: the tensor-core split for p <= 119 on the shapes it takes; *p_lo = 120 when it was launched
+int ozk_split_tc_launch(int is_b, const double* src, const int32_t* vexp, const int32_t* gam, const int32_t* p_dev,
+                        int V, int k, int N, int8_t* out, int32_t* err, cudaStream_t st, int* p_lo);
+
+// Both kernels are launched: the tensor-core one returns at once for p > 119 and this one for p < p_lo, so that the
+// choice follows the device-side p (graph capture included).
 extern "C" int ozk_split_a(const double* A, const int32_t* r, const int32_t* gam, const int32_t* p_dev, int m, int k,
-                           int N, int8_t* Ares, ozk_stream_t stream_) {
-    if (!A || !r || !gam || !p_dev || !Ares) return OZK_ERR_ARG;
+                           int N, int8_t* Ares, int32_t* err, ozk_stream_t stream_) {
+    if (!A || !r || !gam || !p_dev || !Ares || !err) return OZK_ERR_ARG;
     if (m <= 0 || k <= 0 || (k & 31) || N < 1 || N > OZK_NMAX) return OZK_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Ares)) & 15) return OZK_ERR_ARG;
     if ((long long)m * (k >> 5) >= 0x7fffffffLL - (1LL << 24)) return OZK_ERR_ARG;   // chunk indices in 31 bits
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    int p_lo = 0;
+    const int rc = ozk_split_tc_launch(0, A, r, gam, p_dev, m, k, N, Ares, err, st, &p_lo);
+    if (rc != OZK_OK) return rc;
     const long long tasks = ((long long)m * (k >> 5) + 7) / 8;
     if (N > 16 && N <= 20)
-        split_kernel<false, true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares);
+        split_kernel<false, true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares, p_lo);
     else
-        split_kernel<false, false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares);
+        split_kernel<false, false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(A, r, gam, p_dev, m, k, N, Ares, p_lo);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }
 
 extern "C" int ozk_split_b(const double* B, const int32_t* c, const int32_t* gam, const int32_t* p_dev, int k, int n,
-                           int N, int8_t* Bres, ozk_stream_t stream_) {
-    if (!B || !c || !gam || !p_dev || !Bres) return OZK_ERR_ARG;
+                           int N, int8_t* Bres, int32_t* err, ozk_stream_t stream_) {
+    if (!B || !c || !gam || !p_dev || !Bres || !err) return OZK_ERR_ARG;
     if (n <= 0 || k <= 0 || (k & 31) || (n & 31) || N < 1 || N > OZK_NMAX) return OZK_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(Bres) & 15) return OZK_ERR_ARG;
     if ((long long)n * (k >> 5) >= 0x7fffffffLL - (1LL << 24)) return OZK_ERR_ARG;   // chunk indices in 31 bits
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+    int p_lo = 0;
+    const int rc = ozk_split_tc_launch(1, B, c, gam, p_dev, n, k, N, Bres, err, st, &p_lo);
+    if (rc != OZK_OK) return rc;
     const long long tasks = (long long)(n / 8) * (k >> 5);
     if (N > 16 && N <= 20)
-        split_kernel<true, true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres);
+        split_kernel<true, true><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres, p_lo);
     else
-        split_kernel<true, false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres);
+        split_kernel<true, false><<<split_blocks(tasks), kWarps * 32, 0, st>>>(B, c, gam, p_dev, n, k, N, Bres, p_lo);
     OZK_CHECK_LAUNCH();
     return OZK_OK;
 }

@@ -203,6 +203,38 @@ __device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t* v) {
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
         : "r"(taddr));
 }
+// 32 lanes x 4 / 2 / 1 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_ld_32x32b_x4(uint32_t taddr, uint32_t* v) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_32x32b_x2(uint32_t taddr, uint32_t* v) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(v[0]), "=r"(v[1]) : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_32x32b_x1(uint32_t taddr, uint32_t* v) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v[0]) : "r"(taddr));
+}
+// NC consecutive columns starting at taddr, as loads of 16, 8, 4, 2, 1 columns in that order (each load starts at
+// a multiple of its width when taddr's column is a multiple of 16)
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* v) {
+    if constexpr (NC >= 16) {
+        tmem_ld_32x32b_x16(taddr, v);
+        tmem_ld_cols<NC - 16>(taddr + 16u, v + 16);
+    } else if constexpr (NC >= 8) {
+        tmem_ld_32x32b_x8(taddr, v);
+        tmem_ld_cols<NC - 8>(taddr + 8u, v + 8);
+    } else if constexpr (NC >= 4) {
+        tmem_ld_32x32b_x4(taddr, v);
+        tmem_ld_cols<NC - 4>(taddr + 4u, v + 4);
+    } else if constexpr (NC >= 2) {
+        tmem_ld_32x32b_x2(taddr, v);
+        tmem_ld_cols<NC - 2>(taddr + 2u, v + 2);
+    } else if constexpr (NC == 1) {
+        tmem_ld_32x32b_x1(taddr, v);
+    }
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // UMMA shared-memory descriptor for a K-major tile stored with the 128-byte swizzle (rows of 128 bytes, 8-row

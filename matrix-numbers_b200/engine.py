@@ -382,12 +382,13 @@ class OzakiCRT:
         launched = 0
         if with_A:
             check(self.lib.ozk_split_a(ptr(A_rows), ptr(r_rows), ptr(b.gam), ptr(b.p_core), rows, k, N,
-                                       ptr(b.planes_A), st), "ozk_split_a")
-            launched += 1
+                                       ptr(b.planes_A), ptr(b.error_word), st), "ozk_split_a")
+            launched += _lib.split_kernels(A_rows, b.planes_A, rows, k, False)
         if with_B:
-            check(self.lib.ozk_split_b(ptr(B), ptr(b.c), ptr(b.gam), ptr(b.p_core), k, n, N, ptr(b.planes_B), st),
+            check(self.lib.ozk_split_b(ptr(B), ptr(b.c), ptr(b.gam), ptr(b.p_core), k, n, N, ptr(b.planes_B),
+                                       ptr(b.error_word), st),
                   "ozk_split_b")
-            launched += 1
+            launched += _lib.split_kernels(B, b.planes_B, n, k, True)
         mark("residues")
         check(self.lib.ozk_gemm_residues(ptr(b.planes_A), ptr(b.planes_B), rows, n, k, N, ptr(b.planes_X),
                                          ptr(b.error_word), st), "ozk_gemm_residues")

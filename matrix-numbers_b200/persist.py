@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import torch
 
+from . import _lib
 from ._lib import check, ptr
 from .engine import DEV, _stream_handle
 
@@ -49,9 +50,10 @@ class PersistA:
         check(E.lib.ozk_stats_rows(ptr(A), m, k, ptr(b["gam"]), ptr(b["r"]), ptr(b["sA"]), ptr(b["nA"]), st),
               "ozk_stats_rows")
         b["pdev"].fill_(self.p)
-        check(E.lib.ozk_split_a(ptr(A), ptr(b["r"]), ptr(b["gam"]), ptr(b["pdev"]), m, k, self.N, ptr(b["Ares"]), st),
+        check(E.lib.ozk_split_a(ptr(A), ptr(b["r"]), ptr(b["gam"]), ptr(b["pdev"]), m, k, self.N, ptr(b["Ares"]),
+                                ptr(b["err"]), st),
               "ozk_split_a")
-        E.launches += 2
+        E.launches += 1 + _lib.split_kernels(A, b["Ares"], m, k, False)
 
     def _stats_B(self, B):
         """B's column statistics for gamma = 0, then the forced rule (N, p): the device p drops (and the fallback

@@ -215,10 +215,14 @@ def dev_split(pkg, torch, A, B, st, p, N):
     pd = torch.tensor([p], dtype=torch.int32, device="cuda")
     Ar = torch.empty((N, m, k), dtype=torch.int8, device="cuda")
     Br = torch.empty((N, n, k), dtype=torch.int8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
-    pkg._lib.check(L.ozk_split_a(ptr(A), ptr(st["r"]), ptr(st["gam"]), ptr(pd), m, k, N, ptr(Ar), s), "split_a")
-    pkg._lib.check(L.ozk_split_b(ptr(B), ptr(st["c"]), ptr(st["gam"]), ptr(pd), k, n, N, ptr(Br), s), "split_b")
+    pkg._lib.check(L.ozk_split_a(ptr(A), ptr(st["r"]), ptr(st["gam"]), ptr(pd), m, k, N, ptr(Ar), ptr(err), s),
+                   "split_a")
+    pkg._lib.check(L.ozk_split_b(ptr(B), ptr(st["c"]), ptr(st["gam"]), ptr(pd), k, n, N, ptr(Br), ptr(err), s),
+                   "split_b")
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     return Ar.cpu().numpy(), Br.cpu().numpy()
 
 
@@ -254,7 +258,8 @@ def test_split_all_digit_widths(pkg, oracle, torch_mod, p):
 # plane-count boundary of the 16-modulus row tiles, both byte-string widths
 @pytest.mark.parametrize("m,k,n,N,p", [(12, 96, 32, 6, 40), (20, 64, 64, 8, 58), (36, 32, 96, 9, 60),
                                        (12, 160, 32, 16, 70), (44, 96, 32, 17, 67), (8, 224, 64, 24, 90),
-                                       (28, 96, 32, 25, 119), (12, 96, 64, 20, 120), (16, 32, 32, 31, 150)])
+                                       (28, 96, 32, 25, 119), (12, 96, 64, 20, 120), (16, 32, 32, 31, 150),
+                                       (24, 64, 32, 3, 50), (16, 96, 64, 1, 45), (40, 160, 96, 13, 104)])
 def test_split_ragged(pkg, oracle, torch_mod, m, k, n, N, p):
     torch = torch_mod
     A, B = pkg.make_inputs(m, k, n, 1.5, seed=m + k + N)
@@ -282,6 +287,22 @@ def test_split_packed_tail(pkg, oracle, torch_mod, m, k, n, N):
         Ar, Br = dev_split(pkg, torch, Ad, Bd, st, p, N)
         assert np.array_equal(Ar, oracle.split_A(A, sto["r"], sto["gam"], p, N)), p
         assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, N)), p
+
+
+# many tiles per CTA of the tensor-core split (its load ring and both string buffers wrap around several times),
+# narrow and wide digit ranges (p <= 100 and 101 <= p <= 119)
+@pytest.mark.parametrize("N,p", [(18, 67), (20, 110), (16, 58)])
+def test_split_many_tiles(pkg, oracle, torch_mod, N, p):
+    torch = torch_mod
+    m, k, n = 2048, 1536, 1024
+    A, B = pkg.make_inputs(m, k, n, 2.0, seed=N + p)
+    A[5, 7], B[9, 3] = -0.0, 4e-310
+    Ad, Bd = T(torch, A), T(torch, B)
+    st = dev_stats(pkg, torch, Ad, Bd)
+    sto = oracle.stats(A, B, True)
+    Ar, Br = dev_split(pkg, torch, Ad, Bd, st, p, N)
+    assert np.array_equal(Ar, oracle.split_A(A, sto["r"], sto["gam"], p, N))
+    assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, N))
 
 
 # ------------------------------------------------------------------------------------------------ INT8 products

@@ -91,7 +91,7 @@ def test_capi_host_calls_without_device(pkg):
     assert lib.ozk_stats_workspace_bytes(64, 64, 64) > 0
     assert lib.ozk_stats_workspace_bytes(0, 64, 64) == 0
     # argument validation happens before any device work: null pointers are rejected with OZK_ERR_ARG
-    assert lib.ozk_split_a(None, None, None, None, 4, 32, 16, None, None) == -1
+    assert lib.ozk_split_a(None, None, None, None, 4, 32, 16, None, None, None) == -1
     assert lib.ozk_gemm_residues(None, None, 4, 32, 32, 16, None, None, None) == -1
     assert lib.ozk_reconstruct(None, None, None, None, 4, 32, 16, None, None, None) == -1
     assert lib.ozk_wait_selftest(0, 10**6, None, None, None) == -1
