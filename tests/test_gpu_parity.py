@@ -305,6 +305,24 @@ def test_split_many_tiles(pkg, oracle, torch_mod, N, p):
     assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, N))
 
 
+# B 8 bytes off a 16-byte boundary: ozk_split_b keeps the general kernel for it (the tensor-core split loads B by TMA,
+# which needs a 16-byte aligned base), A still takes the tensor-core path; both bit-exact
+def test_split_unaligned_B_uses_general_kernel(pkg, oracle, torch_mod):
+    torch = torch_mod
+    m, k, n, N, p = 96, 256, 64, 18, 67
+    A, B = pkg.make_inputs(m, k, n, 2.0, seed=5)
+    Ad = T(torch, A)
+    store = torch.empty(k * n + 1, dtype=torch.float64, device="cuda")
+    Bd = store[1:].view(k, n)
+    Bd.copy_(T(torch, B))
+    assert Bd.data_ptr() % 16 == 8
+    st = dev_stats(pkg, torch, Ad, T(torch, B))             # the statistics entry points want aligned operands
+    sto = oracle.stats(A, B, True)
+    Ar, Br = dev_split(pkg, torch, Ad, Bd, st, p, N)
+    assert np.array_equal(Ar, oracle.split_A(A, sto["r"], sto["gam"], p, N))
+    assert np.array_equal(Br, oracle.split_B(B, sto["c"], sto["gam"], p, N))
+
+
 # ------------------------------------------------------------------------------------------------ INT8 products
 def rand_planes(rng, N, rows, k):
     return rng.integers(-128, 128, size=(N, rows, k), dtype=np.int64).astype(np.int8)
