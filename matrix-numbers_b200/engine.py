@@ -170,7 +170,8 @@ class Workspace:
 
     def fetch(self, stream=None):
         """Copy the decision block and the rule's auxiliary outputs to the host (one synchronisation) -> (Decision,
-        control words, aux list).  Raises OzkError if an INT8 GEMM launch has set the device error word."""
+        control words, aux list).  Raises OzkError if a split, INT8 product or reconstruction launch has set the device
+        error word."""
         s = torch.cuda.current_stream() if stream is None else stream
         with torch.cuda.stream(s):
             self._h_control.copy_(self.control, non_blocking=True)
@@ -184,8 +185,8 @@ class Workspace:
     @staticmethod
     def raise_on_device_error(word: int):
         if word:
-            raise _lib.OzkError(f"device error flag {word:#x} raised by a product or reconstruction launch (a bounded "
-                                "wait ran out); the results of that call are invalid")
+            raise _lib.OzkError(f"device error flag {word:#x} raised by a split, product or reconstruction launch (a "
+                                "bounded wait ran out); the results of that call are invalid")
 
     def host_stats(self):
         """(statistics dict of numpy arrays, non-finite flag) read from the device (synchronises)."""
@@ -340,7 +341,8 @@ class OzakiCRT:
         return 11 if (req.forced or req.certify) else 12
 
     def check_errors(self):
-        """Raise if any INT8 GEMM launch of this engine reported a device-side error (synchronises)."""
+        """Raise if any split, INT8 product or reconstruction launch of this engine reported a device-side error
+        (synchronises)."""
         for ws in self.bufs.values():
             ws.fetch()
 

@@ -621,3 +621,68 @@ def test_ozk_core_c_abi_equals_engine_core(pkg, oracle, engine, torch_mod, shape
         assert torch.equal(C, C_ref), skip_a
     st_o = oracle.stats(A, B, True)
     np.testing.assert_array_equal(C.cpu().numpy().view(np.uint64), oracle.core(A, B, st_o, N, p).view(np.uint64))
+
+
+def test_host_paths_raise_on_device_error_word(pkg, torch_mod):
+    """A device error word set by a bounded wait that ran out (split, products or reconstruction) makes the
+    host-buffer entry points raise instead of returning C: here the word is set by hand between calls."""
+    torch = torch_mod
+    A, B = pkg.make_inputs(128, 128, 128, 0.5, seed=3)
+    E = pkg.OzakiCRT()
+    Ah, Bh = torch.from_numpy(A).pin_memory(), torch.from_numpy(B).pin_memory()
+    C, _ = E.run_host(Ah, Bh)
+    Cd, _ = E.run(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+    assert torch.equal(C, Cd.cpu())
+    for ws in E.bufs.values():
+        ws.error_word.fill_(16)                                  # OZK_DEVERR_TIMEOUT_SPLIT
+    with pytest.raises(pkg._lib.OzkError):
+        E.run_host(Ah, Bh)
+    with pytest.raises(pkg._lib.OzkError):
+        E.run_host_many([(Ah, Bh, None), (Ah, Bh, None)])
+    with pytest.raises(pkg._lib.OzkError):
+        E.check_errors()
+
+
+_GENERAL_SPLIT_CHILD = r"""
+import os, sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+sys.path.insert(0, os.path.join(sys.argv[1], "oracle"))
+import __graft_entry__
+import oracle
+pkg = __graft_entry__.load_package()
+oracle.build()
+L, ptr = pkg._lib.lib(), pkg._lib.ptr
+for (m, k, n, N, p) in [(96, 160, 64, 18, 67), (40, 96, 32, 13, 104), (64, 256, 96, 20, 58)]:
+    A, B = pkg.make_inputs(m, k, n, 2.0, seed=m + N)
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    st = {x: torch.empty(m if x in ("r", "sA", "nA") else (n if x in ("c", "sB", "nB") else (k if x == "gam" else 1)),
+                         dtype=torch.float64 if x[0] in "sn" else torch.int32, device="cuda")
+          for x in ("gam", "r", "c", "sA", "nA", "sB", "nB", "flag")}
+    ws = torch.empty(L.ozk_stats_workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    pkg._lib.check(L.ozk_stats(ptr(Ad), ptr(Bd), m, n, k, 1, *(ptr(st[x]) for x in ("gam", "r", "c", "sA", "nA", "sB", "nB", "flag")),
+                               ptr(ws), ws.numel(), s), "stats")
+    pd = torch.tensor([p], dtype=torch.int32, device="cuda"); err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    Ar = torch.empty((N, m, k), dtype=torch.int8, device="cuda"); Br = torch.empty((N, n, k), dtype=torch.int8, device="cuda")
+    pkg._lib.check(L.ozk_split_a(ptr(Ad), ptr(st["r"]), ptr(st["gam"]), ptr(pd), m, k, N, ptr(Ar), ptr(err), s), "a")
+    pkg._lib.check(L.ozk_split_b(ptr(Bd), ptr(st["c"]), ptr(st["gam"]), ptr(pd), k, n, N, ptr(Br), ptr(err), s), "b")
+    torch.cuda.synchronize()
+    sto = oracle.stats(A, B, True)
+    assert np.array_equal(Ar.cpu().numpy(), oracle.split_A(A, sto["r"], sto["gam"], p, N)), (m, k, n, N, p)
+    assert np.array_equal(Br.cpu().numpy(), oracle.split_B(B, sto["c"], sto["gam"], p, N)), (m, k, n, N, p)
+    assert int(err.item()) == 0
+print("general split ok")
+"""
+
+
+def test_general_split_kernel_for_small_p(oracle, torch_mod):
+    """OZK_SPLIT_TC=0 (read once per process, hence a child process) keeps split.cu's kernel for p <= 119 too: it
+    stays bit-exact against the oracle, as the tensor-core kernel is."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, OZK_SPLIT_TC="0")
+    r = subprocess.run([sys.executable, "-c", _GENERAL_SPLIT_CHILD, root], env=env, cwd=root, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and "general split ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
