@@ -25,10 +25,13 @@ Where the operands start.  ``run`` takes pre-placed blocks (each rank already ho
 B).  Two more entry points move the operands over NCCL inside the call, on a row-block grid (S = 1):
 
 * ``run_broadcast_b`` -- A's and C's row blocks live on their owners; B lives on one root rank and is broadcast as
-  FP64 (k n 8 bytes) before the statistics.  Broadcasting the FP64 operand moves fewer bytes than its N residue
-  planes would (N k n, N = 16-20), and every rank splits B itself.
-* ``run_from_root`` -- A, B (and C) live on the root only: A's row blocks are scattered, B broadcast, and (with
-  ``gather=True``) the row blocks of C gathered back into the root's C.
+  FP64 (k n 8 bytes).  Broadcasting the FP64 operand moves fewer bytes than its N residue planes would (N k n,
+  N = 16-20), and every rank splits B itself.  The broadcast runs on a second communicator over the same ranks while
+  the statistics proceed: the root computes B's row maxima and column statistics from its own copy and sends those
+  vectors, every rank computes its rows' statistics, and B is waited for only before the probe product.
+* ``run_from_root`` -- A, B (and C) live on the root only: B's broadcast starts, A's row blocks are scattered, the
+  statistics overlap the broadcast as above, and (with ``gather=True``) the row blocks of C are gathered back into
+  the root's C.
 
 Every collective is NCCL's (no peer-memory loads, no TMA multicast): the exchanges are plain operand moves and small
 statistics vectors, with no computation to fuse them with.  ``events`` (a list) receives (name, CUDA event) marks
@@ -87,19 +90,23 @@ class CudaOps:
         self.engine.launches += 1
         return out
 
-    def local_stats(self, A, B, colmax, rowmax, inside):
-        """gamma from the global maxima, then this rank's row statistics of A and column statistics of B."""
+    def local_stats(self, A, B, colmax, rowmax, inside, cols=None):
+        """gamma from the global maxima, then this rank's row statistics of A and column statistics of B.  With
+        B None (``cols`` columns) the column statistics are left to the caller (they arrive from the rank that
+        holds B)."""
         rows, k = A.shape
-        cols = B.shape[1]
+        cols = B.shape[1] if B is not None else cols
         b = self.engine.buffers(rows, cols, k, 20)
         st = self._stream()
         check(self.lib.ozk_stats_gamma(ptr(colmax), ptr(rowmax), k, 1 if inside else 0, ptr(b["gam"]), ptr(b["flag"]),
                                        st), "ozk_stats_gamma")
         check(self.lib.ozk_stats_rows(ptr(A), rows, k, ptr(b["gam"]), ptr(b["r"]), ptr(b["sA"]), ptr(b["nA"]), st),
               "ozk_stats_rows")
-        check(self.lib.ozk_stats_cols(ptr(B), k, cols, ptr(b["gam"]), ptr(b["c"]), ptr(b["sB"]), ptr(b["nB"]),
-                                      ptr(b["ws_stats"]), b["ws_stats"].numel(), st), "ozk_stats_cols")
-        self.engine.launches += 4
+        self.engine.launches += 2
+        if B is not None:
+            check(self.lib.ozk_stats_cols(ptr(B), k, cols, ptr(b["gam"]), ptr(b["c"]), ptr(b["sB"]), ptr(b["nB"]),
+                                          ptr(b["ws_stats"]), b["ws_stats"].numel(), st), "ozk_stats_cols")
+            self.engine.launches += 2
         return {"gam": b["gam"], "r": b["r"], "sA": b["sA"], "nA": b["nA"], "c": b["c"], "sB": b["sB"], "nB": b["nB"],
                 "flag": b["flag"], "_b": b}
 
@@ -200,6 +207,10 @@ class DistributedOzakiCRT:
         self.ops = ops if ops is not None else CudaOps()
         self.probe = {}
         self._recv = {}                                       # receive buffers of the operand moves, per name
+        # a second communicator over the same ranks for the bulk operand moves (B's broadcast), so that the small
+        # statistics collectives run beside it instead of queueing behind it; created here, on every rank alike
+        ranks = dist.get_process_group_ranks(group) if group is not None else list(range(self.world))
+        self.bulk = dist.new_group(ranks=ranks)
 
     @property
     def engine(self):
@@ -265,9 +276,8 @@ class DistributedOzakiCRT:
         if self.rank == root:
             assert B.is_contiguous() and B.dtype == torch.float64
         self._mark(events, "start")
-        dist.broadcast(Bl, src=root, group=self.group)
-        self._mark(events, "broadcast B")
-        return self.run(A, Bl, C, events=events, **kw)
+        work = dist.broadcast(Bl, src=root, group=self.bulk, async_op=True)
+        return self._run_b_on_root(A, Bl, C, root, work, events, **kw)
 
     def run_from_root(self, A=None, B=None, C=None, root=0, gather=True, events=None, **kw):
         """C = A B with A (m x k) and B (k x n) only on rank ``root``: A's row blocks are scattered, B broadcast,
@@ -287,16 +297,55 @@ class DistributedOzakiCRT:
             if C is None and gather:
                 C = torch.empty((m, n), dtype=torch.float64, device=dev)
         self._mark(events, "start")
+        work = dist.broadcast(Bl, src=root, group=self.bulk, async_op=True)
         dist.scatter(Ab, list(A.split(rows)) if self.rank == root else None, src=root, group=self.group)
         self._mark(events, "scatter A")
-        dist.broadcast(Bl, src=root, group=self.group)
-        self._mark(events, "broadcast B")
-        _, info = self.run(Ab, Bl, Cb, events=events, **kw)
+        _, info = self._run_b_on_root(Ab, Bl, Cb, root, work, events, **kw)
         if not gather:
             return Cb, info
         dist.gather(Cb, list(C.split(rows)) if self.rank == root else None, dst=root, group=self.group)
         self._mark(events, "gather C")
         return (C if self.rank == root else Cb), info
+
+    def _run_b_on_root(self, A, Bl, C, root, pending, events, tau=2.0 ** -52, force_N=None, inside=True, seed=0,
+                       force_p=None, safety=2.0, config=None, certify=False):
+        """``run`` on a row-block grid while B is still arriving from ``root`` (``pending``: the handle of its
+        broadcast on the bulk communicator).  The root computes B's row maxima and column statistics from its own
+        copy while the broadcast runs and sends those vectors (3 n values); every rank computes its rows' statistics
+        meanwhile, and waits for B only before the probe product and the core.  Same collectives in the same order
+        on every rank; the decision and C equal ``run``'s bit for bit."""
+        if config is not None:
+            force_N, force_p = int(config["N"]), config.get("p")
+        rows, k = A.shape
+        n = Bl.shape[1]
+        assert Bl.shape[0] == k and rows % 4 == 0 and n % 32 == 0 and k % 32 == 0, "shape rule (per rank)"
+        m = rows * self.R
+        is_root = self.rank == root
+        if C is None:
+            C = torch.empty((rows, n), dtype=torch.float64, device=A.device)
+        # 1. global maxima: B's row maxima from the root only (zeros, the identity of MAX on the non-negative bit
+        #    patterns, elsewhere)
+        cm = self.ops.colmax(A)
+        rm = self.ops.rowmax(Bl) if is_root else torch.zeros_like(cm)
+        mx = torch.cat([cm, rm])
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=self.group)
+        self._mark(events, "maxima + all_reduce")
+        # 2. rows' statistics everywhere; B's column statistics on the root, then broadcast
+        st = self.ops.local_stats(A, Bl if is_root else None, mx[:k], mx[k:], inside, cols=n)
+        glob = self.ops.global_stats(m, n, A.device)
+        for x in ("r", "sA", "nA"):
+            glob[x].copy_(self._gather(st[x], m, 1, self.R))
+        for x in ("c", "sB", "nB"):
+            if is_root:
+                glob[x].copy_(st[x])
+            dist.broadcast(glob[x], src=root, group=self.group)
+            if not is_root:
+                st[x].copy_(glob[x])
+        self._mark(events, "statistics + all_gather")
+        pending.wait()
+        self._mark(events, "broadcast B (rest)")
+        return self._decide_and_core(A, Bl, C, st, glob, m, n, k, rows * self.a, 0, tau, force_N, seed, force_p,
+                                     safety, certify, events)
 
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, safety=2.0,
             config=None, certify=False, events=None):
@@ -323,6 +372,13 @@ class DistributedOzakiCRT:
         for x in ("c", "sB", "nB"):
             glob[x].copy_(self._gather(st[x], n, 1, self.S))
         self._mark(events, "statistics + all_gather")
+        return self._decide_and_core(A, B, C, st, glob, m, n, k, row_begin, col_begin, tau, force_N, seed, force_p,
+                                     safety, certify, events)
+
+    def _decide_and_core(self, A, B, C, st, glob, m, n, k, row_begin, col_begin, tau, force_N, seed, force_p, safety,
+                         certify, events):
+        """Steps 3 (probe or certificate, the same decision on every rank) and the local core."""
+        rows, cols = A.shape[0], B.shape[1]
         if certify and force_N is None:
             # 3'. full-matrix certificate: minimum over the blocks, then the same decision everywhere
             xb, unc = self.ops.certificate_block(A, B, st, tau, safety)

@@ -38,8 +38,10 @@ class OracleOps:
     def rowmax(self, B):
         return torch.from_numpy(self.O.rowmax(B.numpy()).copy())
 
-    def local_stats(self, A, B, colmax, rowmax, inside):
-        st = self.O.stats_given_maxima(A.numpy(), B.numpy(), colmax.numpy(), rowmax.numpy(), inside)
+    def local_stats(self, A, B, colmax, rowmax, inside, cols=None):
+        # B None: column statistics come from the rank that holds B (placeholders of the right size here)
+        Bn = B.numpy() if B is not None else np.zeros((A.shape[1], cols))
+        st = self.O.stats_given_maxima(A.numpy(), Bn, colmax.numpy(), rowmax.numpy(), inside)
         out = {x: torch.from_numpy(np.ascontiguousarray(st[x])) for x in ("gam", "r", "sA", "nA", "c", "sB", "nB")}
         out["flag"] = torch.tensor([st["flag"]], dtype=torch.int32)
         out["_np"] = st
