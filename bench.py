@@ -413,19 +413,27 @@ def main():
                 return C, {"N": PA.N, "p": PA.p}
         launches_of = lambda: E.launches  # noqa: E731
     else:
-        # headline on N GPUs: C row blocks; A's and C's row blocks live on their owners, B lives on rank 0 only and
-        # is broadcast (FP64) over NCCL inside every timed call
+        # headline on N GPUs: blocks of C on the default grid (R x S, S = 2 from 4 ranks on); A's row block a lives on
+        # the ranks of grid row a and C's blocks on their ranks; B lives on rank 0 only and is sent (FP64) over NCCL
+        # inside every timed call -- whole to every rank on a row grid, column block b to grid column b otherwise
         assert args.mode in ("sampled", "certified"), "--mode config / persist are single-GPU"
         cert = args.mode == "certified"
-        R, S = world, 1
-        rows, cols = m // R, n
-        assert rows % 4 == 0, "block shape rule"
-        A = torch.from_numpy(np.ascontiguousarray(A_host[rank * rows:(rank + 1) * rows])).to(dev)
+        from matrix_numbers_b200.distributed import default_grid
+        R, S = default_grid(world)
+        ga, gb = divmod(rank, S)
+        rows, cols = m // R, n // S
+        assert rows % 4 == 0 and cols % 32 == 0, "block shape rule"
+        A = torch.from_numpy(np.ascontiguousarray(A_host[ga * rows:(ga + 1) * rows])).to(dev)
         B_root = torch.from_numpy(B_host).to(dev) if rank == 0 else None
-        C = torch.empty((rows, n), dtype=torch.float64, device=dev)
+        # rank 0 keeps B as its S contiguous column blocks (the layout the column groups receive)
+        B_parts = ([torch.from_numpy(np.ascontiguousarray(B_host[:, q * cols:(q + 1) * cols])).to(dev)
+                    for q in range(S)] if (rank == 0 and S > 1) else B_root)
+        C = torch.empty((rows, cols), dtype=torch.float64, device=dev)
         D = pkg.DistributedOzakiCRT(grid=(R, S))
+        # the ranks of each grid row share A's row block: the end-to-end step uploads half of it on each and gathers
+        row_groups = [dist.new_group([a * S + q for q in range(S)]) for a in range(R)] if S > 1 else None
         engine = D.engine
-        call = lambda ev=None: D.run_broadcast_b(A, B_root, C, root=0, force_N=forceN, certify=cert, events=ev)  # noqa: E731
+        call = lambda ev=None: D.run_broadcast_b(A, B_parts, C, root=0, force_N=forceN, certify=cert, events=ev)  # noqa: E731
         launches_of = lambda: D.launches  # noqa: E731
 
     launches0 = launches_of()
@@ -439,9 +447,7 @@ def main():
     if world > 1:
         # beside the headline: the same product with every operand pre-placed (no operand bytes on NVLink), on the
         # default grid; and with A and B on rank 0 only (A scattered, B broadcast, C gathered into rank 0)
-        from matrix_numbers_b200.distributed import default_grid
         gR, gS = default_grid(world)
-        ga, gb = divmod(rank, gS)
         br, bc = m // gR, n // gS
         A_g = torch.from_numpy(np.ascontiguousarray(A_host[ga * br:(ga + 1) * br])).to(dev)
         B_g = torch.from_numpy(np.ascontiguousarray(B_host[:, gb * bc:(gb + 1) * bc])).to(dev)
@@ -459,9 +465,10 @@ def main():
         del A_g, B_g, C_g, Dg
         A_root = torch.from_numpy(A_host).to(dev) if rank == 0 else None
         C_root = torch.empty((m, n), dtype=torch.float64, device=dev) if rank == 0 else None
+        Dr = pkg.DistributedOzakiCRT(grid=(world, 1))
         t_root, _, st_root, _ = timed_calls(
             torch, dist,
-            lambda ev=None: D.run_from_root(A_root, B_root, C_root, root=0, force_N=forceN, certify=cert, events=ev),
+            lambda ev=None: Dr.run_from_root(A_root, B_root, C_root, root=0, force_N=forceN, certify=cert, events=ev),
             args.steps, args.warmup, world, stream, stage_events=True)
         extra["from_root"] = {"value": flops / t_root / 1e12, "ms_per_step": t_root * 1e3,
                               "what": "A and B on rank 0 only: A's row blocks scattered, B broadcast, C's row "
@@ -480,7 +487,7 @@ def main():
     Nplanes = info.get("N") or forceN
     prof = {}
     b = engine.buffers(rows, cols, k, Nplanes)
-    B_core = B if world == 1 else D._recv.get("B", B_root)
+    B_core = B if world == 1 else D.last_b
     for _ in range(3):
         engine.core(A, B_core, b, Nplanes, C, prof=prof)
     t_gemm = prof["gemm+reduce"] / 3
@@ -530,8 +537,18 @@ def main():
     # end to end through the public API with host buffers (pinned), H2D + D2H inside the timed region
     e2e = None
     if args.e2e_steps > 0:
-        Ah = torch.from_numpy(np.ascontiguousarray(A_host[rank * rows:(rank + 1) * rows])).pin_memory()
-        Bh = torch.from_numpy(B_host).pin_memory() if (world == 1 or rank == 0) else None
+        ra, rb = divmod(rank, S)
+        sub_rows = rows // S                                   # this rank's share of the upload of A's row block
+        Ah = torch.from_numpy(np.ascontiguousarray(
+            A_host[ra * rows + rb * sub_rows:ra * rows + (rb + 1) * sub_rows])).pin_memory()
+        A_half = torch.empty((sub_rows, k), dtype=torch.float64, device=dev) if S > 1 else None
+        if world == 1:
+            Bh = torch.from_numpy(B_host).pin_memory()
+        elif rank == 0:
+            Bh = [torch.from_numpy(np.ascontiguousarray(B_host[:, q * cols:(q + 1) * cols])).pin_memory()
+                  for q in range(S)] if S > 1 else torch.from_numpy(B_host).pin_memory()
+        else:
+            Bh = None
         Ch = torch.empty((rows, cols), dtype=torch.float64).pin_memory()
         if world == 1 and args.mode == "sampled":
             E.run_host(Ah, Bh, Ch, force_N=forceN)             # warm-up of the host-buffer path
@@ -557,17 +574,26 @@ def main():
         else:
             # every step: H2D of this rank's A rows (and of B on rank 0), the headline call, D2H of the C rows
             def host_step(ev=None):
-                A.copy_(Ah, non_blocking=True)
+                if S > 1:
+                    A_half.copy_(Ah, non_blocking=True)
+                    dist.all_gather_into_tensor(A, A_half, group=row_groups[ra])
+                else:
+                    A.copy_(Ah, non_blocking=True)
                 if world > 1 and rank == 0:
-                    B_root.copy_(Bh, non_blocking=True)
+                    if S > 1:
+                        for q in range(S):
+                            B_parts[q].copy_(Bh[q], non_blocking=True)
+                    else:
+                        B_root.copy_(Bh, non_blocking=True)
                 elif world == 1:
                     B.copy_(Bh, non_blocking=True)
                 out = call(None)
                 Ch.copy_(C, non_blocking=True)
                 return out
             t_e2e, _, _, _ = timed_calls(torch, dist, host_step, args.e2e_steps, 1, world, stream)
-            api = ("per rank: H2D of its A rows (rank 0 also B), DistributedOzakiCRT.run_broadcast_b, D2H of its C "
-                   "rows" if world > 1 else "H2D of A and B, OzakiCRT.run_fast, D2H of C")
+            api = ("per rank: H2D of its share of A's row block (the ranks of a grid row gather it over NCCL), rank 0 "
+                   "also H2D of B, DistributedOzakiCRT.run_broadcast_b, D2H of its block of C" if world > 1
+                   else "H2D of A and B, OzakiCRT.run_fast, D2H of C")
             single = None
         e2e = {"value": flops / t_e2e / 1e12, "unit": "TFLOPS", "ms_per_step": t_e2e * 1e3, "api": api,
                "h2d_bytes_per_step": (m * k + k * n) * 8, "d2h_bytes_per_step": m * n * 8}
@@ -594,8 +620,9 @@ def main():
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "accuracy": acc, "clocks": clocks,
                 "gpu_launches": launches, "hbm_peak_gbs": hbm_peak, "peaks": peak_src}
         if world > 1:
-            line["operands"] = ("A's and C's row blocks on their ranks; B on rank 0, broadcast (FP64) over NCCL "
-                                "inside every timed call")
+            line["operands"] = ("A's row block a on the ranks of grid row a, C's blocks on their ranks; B on rank 0, "
+                                "sent (FP64) over NCCL inside every timed call: whole to every rank on a row grid, "
+                                "column block b to the ranks of grid column b otherwise")
             line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -22,16 +22,19 @@ the certified-mode decision from the same numbers.  The result equals the single
 the CRT stage is exact).
 
 Where the operands start.  ``run`` takes pre-placed blocks (each rank already holds its rows of A and its columns of
-B).  Two more entry points move the operands over NCCL inside the call, on a row-block grid (S = 1):
+B).  Two more entry points move the operands over NCCL inside the call:
 
-* ``run_broadcast_b`` -- A's and C's row blocks live on their owners; B lives on one root rank and is broadcast as
-  FP64 (k n 8 bytes).  Broadcasting the FP64 operand moves fewer bytes than its N residue planes would (N k n,
-  N = 16-20), and every rank splits B itself.  The broadcast runs on a second communicator over the same ranks while
-  the statistics proceed: the root computes B's row maxima and column statistics from its own copy and sends those
-  vectors, every rank computes its rows' statistics, and B is waited for only before the probe product.
-* ``run_from_root`` -- A, B (and C) live on the root only: B's broadcast starts, A's row blocks are scattered, the
-  statistics overlap the broadcast as above, and (with ``gather=True``) the row blocks of C are gathered back into
-  the root's C.
+* ``run_broadcast_b`` -- A's row block a lives on the ranks of grid row a and C's blocks on their owners; B lives on
+  one root rank and is sent as FP64: whole to every rank on a row-block grid (S = 1), column block b to the ranks of
+  grid column b on an R x S grid (one communicator per column group, the root in each; the root's egress stays one
+  copy of B, and every rank splits only its n / S columns of B instead of all of them).  Sending the FP64 operand
+  moves fewer bytes than its N residue planes would (N k n, N = 16-20).  The sends run on their own communicators
+  while the statistics proceed: the root computes B's row maxima and column statistics from its own copy and
+  broadcasts those vectors, every rank computes its rows' statistics, and B is waited for only before the probe
+  product.
+* ``run_from_root`` -- A, B (and C) live on the root only (row-block grid): B's broadcast starts, A's row blocks are
+  scattered, the statistics overlap the broadcast as above, and (with ``gather=True``) the row blocks of C are
+  gathered back into the root's C.
 
 Every collective is NCCL's (no peer-memory loads, no TMA multicast): the exchanges are plain operand moves and small
 statistics vectors, with no computation to fuse them with.  ``events`` (a list) receives (name, CUDA event) marks
@@ -109,6 +112,23 @@ class CudaOps:
             self.engine.launches += 2
         return {"gam": b["gam"], "r": b["r"], "sA": b["sA"], "nA": b["nA"], "c": b["c"], "sB": b["sB"], "nB": b["nB"],
                 "flag": b["flag"], "_b": b}
+
+    def col_stats(self, B, st, colmax, rowmax, inside):
+        """Column statistics (c, sB, nB) of all of B (k x n) with this rank's gamma (``st["gam"]``, from the global
+        maxima): the root's share of ``run_broadcast_b``."""
+        k, n = B.shape
+        out = self._glob.get(("cols", n))
+        if out is None:
+            out = {"c": torch.empty(n, dtype=torch.int32, device=B.device),
+                   "sB": torch.empty(n, dtype=torch.float64, device=B.device),
+                   "nB": torch.empty(n, dtype=torch.float64, device=B.device),
+                   "ws": torch.empty(max(1, self.lib.ozk_stats_cols_workspace_bytes(k, n)), dtype=torch.uint8,
+                                     device=B.device)}
+            self._glob[("cols", n)] = out
+        check(self.lib.ozk_stats_cols(ptr(B), k, n, ptr(st["gam"]), ptr(out["c"]), ptr(out["sB"]), ptr(out["nB"]),
+                                      ptr(out["ws"]), out["ws"].numel(), self._stream()), "ozk_stats_cols")
+        self.engine.launches += 2
+        return out
 
     def global_stats(self, m, n, device):
         g = self._glob.get((m, n))
@@ -207,6 +227,7 @@ class DistributedOzakiCRT:
         self.ops = ops if ops is not None else CudaOps()
         self.probe = {}
         self._recv = {}                                       # receive buffers of the operand moves, per name
+        self.last_b = None
         # a second communicator over the same ranks for the bulk operand moves (B's broadcast), so that the small
         # statistics collectives run beside it instead of queueing behind it; created here, on every rank alike
         ranks = dist.get_process_group_ranks(group) if group is not None else list(range(self.world))
@@ -263,21 +284,58 @@ class DistributedOzakiCRT:
                 return t.device
         return getattr(self.ops, "device", torch.device("cpu"))
 
+    def _column_groups(self, root):
+        """Per column block b, the communicator over the root and the ranks of grid column b (the bulk communicator
+        when S = 1).  Created on first use for a root, by every rank in the same order (new_group is collective)."""
+        if self.S == 1:
+            return [self.bulk]
+        groups = self.__dict__.setdefault("_colgroups", {})
+        if root not in groups:
+            base = dist.get_process_group_ranks(self.group) if self.group is not None else list(range(self.world))
+            groups[root] = [dist.new_group(ranks=sorted({base[root]} | {base[a * self.S + b] for a in range(self.R)}))
+                            for b in range(self.S)]
+        return groups[root]
+
     def run_broadcast_b(self, A, B=None, C=None, root=0, events=None, **kw):
-        """This rank's row block of C = A B when B lives only on rank ``root``: B (k x n FP64) is broadcast from the
-        root over NCCL, then the blocks are multiplied as in ``run``.  A (rows x k) is this rank's row block; B is
-        the whole B on the root and ignored elsewhere.  Needs a row-block grid (S = 1)."""
-        assert self.S == 1, "run_broadcast_b needs a row-block grid (S = 1)"
-        dev = self._device_of(A, B)
+        """This rank's block of C = A B when B lives only on rank ``root``: B (k x n FP64) is sent from the root
+        over NCCL, then the blocks are multiplied as in ``run``.  Rank g = a S + b passes A's row block a (rows x k,
+        rows = m / R); on the root B is the whole k x n matrix or, for S > 1, the list of its S contiguous column
+        blocks (k x n / S each; a whole B is cut into such blocks first); elsewhere it is ignored.  On a row-block
+        grid (S = 1) B is broadcast whole; with S > 1 column block b goes to the ranks of grid column b only (the
+        root's egress is still one copy of B; every rank receives, splits and multiplies n / S columns)."""
+        is_root = self.rank == root
+        parts = None
+        if is_root:
+            parts = list(B) if isinstance(B, (list, tuple)) else [B]
+            for t in parts:
+                assert t.is_contiguous() and t.dtype == torch.float64
+        dev = self._device_of(A, *(parts or []))
         k = A.shape[1]
-        k_b, n = self._header([B.shape[0], B.shape[1]] if self.rank == root else [0, 0], root, dev)
+        hdr = [parts[0].shape[0], sum(t.shape[1] for t in parts), len(parts)] if is_root else [0, 0, 0]
+        k_b, n, nparts = self._header(hdr, root, dev)
         assert k_b == k, "A's and B's inner dimensions differ"
-        Bl = B if self.rank == root else self._buffer("B", (k, n), torch.float64, dev)
-        if self.rank == root:
-            assert B.is_contiguous() and B.dtype == torch.float64
+        assert n % self.S == 0, "n must divide into equal column blocks"
+        cols = n // self.S
+        if is_root and self.S > 1 and nparts == 1:
+            whole = parts[0]
+            parts = []
+            for b in range(self.S):
+                blk = self._buffer(f"Bc{b}", (k, cols), torch.float64, dev)
+                blk.copy_(whole[:, b * cols:(b + 1) * cols])
+                parts.append(blk)
+        if is_root:
+            assert len(parts) == self.S and all(tuple(t.shape) == (k, cols) for t in parts), "B's column blocks"
+        groups = self._column_groups(root)
         self._mark(events, "start")
-        work = dist.broadcast(Bl, src=root, group=self.bulk, async_op=True)
-        return self._run_b_on_root(A, Bl, C, root, work, events, **kw)
+        works = []
+        Bl = parts[self.b] if is_root else self._buffer("B", (k, cols), torch.float64, dev)
+        for b in range(self.S):
+            if is_root:
+                works.append(dist.broadcast(parts[b], src=root, group=groups[b], async_op=True))
+            elif b == self.b:
+                works.append(dist.broadcast(Bl, src=root, group=groups[b], async_op=True))
+        self.last_b = Bl                      # this rank's block of B (kept for callers that reuse it)
+        return self._run_b_on_root(A, Bl, parts, n, C, root, works, events, **kw)
 
     def run_from_root(self, A=None, B=None, C=None, root=0, gather=True, events=None, **kw):
         """C = A B with A (m x k) and B (k x n) only on rank ``root``: A's row blocks are scattered, B broadcast,
@@ -300,51 +358,65 @@ class DistributedOzakiCRT:
         work = dist.broadcast(Bl, src=root, group=self.bulk, async_op=True)
         dist.scatter(Ab, list(A.split(rows)) if self.rank == root else None, src=root, group=self.group)
         self._mark(events, "scatter A")
-        _, info = self._run_b_on_root(Ab, Bl, Cb, root, work, events, **kw)
+        _, info = self._run_b_on_root(Ab, Bl, [B] if self.rank == root else None, n, Cb, root, [work], events, **kw)
         if not gather:
             return Cb, info
         dist.gather(Cb, list(C.split(rows)) if self.rank == root else None, dst=root, group=self.group)
         self._mark(events, "gather C")
         return (C if self.rank == root else Cb), info
 
-    def _run_b_on_root(self, A, Bl, C, root, pending, events, tau=2.0 ** -52, force_N=None, inside=True, seed=0,
-                       force_p=None, safety=2.0, config=None, certify=False):
-        """``run`` on a row-block grid while B is still arriving from ``root`` (``pending``: the handle of its
-        broadcast on the bulk communicator).  The root computes B's row maxima and column statistics from its own
-        copy while the broadcast runs and sends those vectors (3 n values); every rank computes its rows' statistics
-        meanwhile, and waits for B only before the probe product and the core.  Same collectives in the same order
-        on every rank; the decision and C equal ``run``'s bit for bit."""
+    def _run_b_on_root(self, A, Bl, B_parts, n, C, root, pending, events, tau=2.0 ** -52, force_N=None, inside=True,
+                       seed=0, force_p=None, safety=2.0, config=None, certify=False):
+        """``run`` while this rank's block of B (``Bl``, k x n / S) is still arriving from ``root`` (``pending``:
+        the handles of the sends on the bulk communicators).  The root computes B's row maxima and column
+        statistics from its own copy (``B_parts``: B's column blocks, in order) while the sends run and broadcasts
+        the column statistics (3 n values); every rank computes its rows' statistics meanwhile, and waits for B
+        only before the probe product.  Same collectives in the same order on every rank; the decision and C equal
+        ``run``'s bit for bit."""
         if config is not None:
             force_N, force_p = int(config["N"]), config.get("p")
         rows, k = A.shape
-        n = Bl.shape[1]
-        assert Bl.shape[0] == k and rows % 4 == 0 and n % 32 == 0 and k % 32 == 0, "shape rule (per rank)"
+        cols = n // self.S
+        assert Bl.shape == (k, cols) and rows % 4 == 0 and cols % 32 == 0 and k % 32 == 0, "shape rule (per rank)"
         m = rows * self.R
+        row_begin, col_begin = rows * self.a, cols * self.b
         is_root = self.rank == root
         if C is None:
-            C = torch.empty((rows, n), dtype=torch.float64, device=A.device)
+            C = torch.empty((rows, cols), dtype=torch.float64, device=A.device)
         # 1. global maxima: B's row maxima from the root only (zeros, the identity of MAX on the non-negative bit
         #    patterns, elsewhere)
         cm = self.ops.colmax(A)
-        rm = self.ops.rowmax(Bl) if is_root else torch.zeros_like(cm)
+        if is_root:
+            rm = self.ops.rowmax(B_parts[0])
+            for part in B_parts[1:]:
+                rm = torch.maximum(rm, self.ops.rowmax(part))
+        else:
+            rm = torch.zeros_like(cm)
         mx = torch.cat([cm, rm])
         dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=self.group)
         self._mark(events, "maxima + all_reduce")
-        # 2. rows' statistics everywhere; B's column statistics on the root, then broadcast
-        st = self.ops.local_stats(A, Bl if is_root else None, mx[:k], mx[k:], inside, cols=n)
+        # 2. rows' statistics everywhere; all of B's column statistics on the root, then broadcast (each rank keeps
+        #    its block's slice for the split)
+        st = self.ops.local_stats(A, None, mx[:k], mx[k:], inside, cols=cols)
         glob = self.ops.global_stats(m, n, A.device)
         for x in ("r", "sA", "nA"):
-            glob[x].copy_(self._gather(st[x], m, 1, self.R))
+            glob[x].copy_(self._gather(st[x], m, self.S, self.R))
+        if is_root:
+            c0 = 0
+            for part in B_parts:
+                cs = self.ops.col_stats(part, st, mx[:k], mx[k:], inside)
+                w = part.shape[1]
+                for x in ("c", "sB", "nB"):
+                    glob[x][c0:c0 + w].copy_(cs[x])
+                c0 += w
         for x in ("c", "sB", "nB"):
-            if is_root:
-                glob[x].copy_(st[x])
             dist.broadcast(glob[x], src=root, group=self.group)
-            if not is_root:
-                st[x].copy_(glob[x])
+            st[x].copy_(glob[x][col_begin:col_begin + cols])
         self._mark(events, "statistics + all_gather")
-        pending.wait()
+        for w in pending:
+            w.wait()
         self._mark(events, "broadcast B (rest)")
-        return self._decide_and_core(A, Bl, C, st, glob, m, n, k, rows * self.a, 0, tau, force_N, seed, force_p,
+        return self._decide_and_core(A, Bl, C, st, glob, m, n, k, row_begin, col_begin, tau, force_N, seed, force_p,
                                      safety, certify, events)
 
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, safety=2.0,

@@ -1,8 +1,8 @@
-"""DistributedOzakiCRT on two GPUs over NCCL (skipped when the machine has fewer than two): the pre-placed grid of C
-blocks, B broadcast from one rank inside the call, and A, B on one rank with scatter / broadcast / gather.  Every C
-must equal the single-GPU product bit for bit, and both ranks must decide the same (N, p).  The ranks are spawned
-child processes, one per GPU; the process group has a short timeout so that a failure ends the test instead of
-hanging it."""
+"""DistributedOzakiCRT over NCCL on two GPUs (skipped when the machine has fewer): the pre-placed grid of C blocks, B
+broadcast from one rank inside the call, and A, B on one rank with scatter / broadcast / gather; and on four GPUs (a
+2 x 2 grid) B's column blocks sent from one rank to their grid columns.  Every C must equal the single-GPU product bit
+for bit, and every rank must decide the same (N, p).  The ranks are spawned child processes, one per GPU; the process
+group has a short timeout so that a failure ends the test instead of hanging it."""
 import os
 import socket
 import sys
@@ -100,3 +100,78 @@ def test_two_ranks_nccl_bit_exact(tmp_path):
     for name in ("pre", "bcast", "root"):
         for r in range(world):
             assert eval(open(os.path.join(tmp_path, f"{name}_{r}.txt")).read()) == want, (name, r)
+
+
+def _worker_grid(rank, world, port, outdir):
+    """2 x 2 grid, B only on rank 0 as its two column blocks: column block b is sent to grid column b."""
+    try:
+        sys.path.insert(0, ROOT)
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        import __graft_entry__
+        pkg = __graft_entry__.load_package()
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        from matrix_numbers_b200.distributed import DistributedOzakiCRT
+        m, k, n = SHAPE
+        A, B = pkg.make_inputs(m, k, n, 2.0, seed=44)
+        R, S = 2, 2
+        a, b = divmod(rank, S)
+        rows, cols = m // R, n // S
+        A_rows = torch.from_numpy(np.ascontiguousarray(A[a * rows:(a + 1) * rows])).to(dev)
+        parts = [torch.from_numpy(np.ascontiguousarray(B[:, q * cols:(q + 1) * cols])).to(dev) for q in range(S)]
+        D = DistributedOzakiCRT(grid=(R, S))
+        C, info = D.run_broadcast_b(A_rows, parts if rank == 0 else None, root=0)
+        C2, info2 = D.run_broadcast_b(A_rows, torch.from_numpy(B).to(dev) if rank == 0 else None, root=0)
+        torch.cuda.synchronize()
+        D.engine.check_errors()
+        np.save(os.path.join(outdir, f"grid_{rank}.npy"), C.cpu().numpy())
+        np.save(os.path.join(outdir, f"grid2_{rank}.npy"), C2.cpu().numpy())
+        with open(os.path.join(outdir, f"grid_{rank}.txt"), "w") as f:
+            f.write(repr(((info["N"], info["p"], info["preq"]), (info2["N"], info2["p"], info2["preq"]))))
+        if rank == 0:
+            E = pkg.OzakiCRT()
+            Cs, i_s = E.run(torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev))
+            np.save(os.path.join(outdir, "single.npy"), Cs.cpu().numpy())
+            with open(os.path.join(outdir, "single.txt"), "w") as f:
+                f.write(repr((i_s["N"], i_s["p"], i_s["p_req"])))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        with open(os.path.join(outdir, f"error_{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+
+
+def test_four_ranks_grid_broadcast_bit_exact(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 4:
+        pytest.skip("needs four GPUs")
+    world = 4
+    ctx = mp.start_processes(_worker_grid, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(timeout=240)
+    alive = [p.is_alive() for p in ctx.processes]
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    assert not any(alive), "a rank did not finish"
+    errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    single = np.load(os.path.join(tmp_path, "single.npy")).view(np.uint64)
+    want = eval(open(os.path.join(tmp_path, "single.txt")).read())
+    for name in ("grid", "grid2"):
+        C = np.concatenate([np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{a * 2 + b}.npy"))
+                                            for b in range(2)], axis=1) for a in range(2)])
+        np.testing.assert_array_equal(C.view(np.uint64), single, err_msg=name)
+    for r in range(world):
+        got = eval(open(os.path.join(tmp_path, f"grid_{r}.txt")).read())
+        assert got[0] == want and got[1] == want, (r, got, want)
