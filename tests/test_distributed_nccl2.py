@@ -55,6 +55,12 @@ def _worker(rank, world, port, outdir):
         A_full = torch.from_numpy(A).to(dev)
         C, info = D.run_from_root(A_full if rank == root else None, B_full if rank == root else None, root=root)
         out["root"] = (C.cpu().numpy(), (info["N"], info["p"], info["preq"]))
+        # a 1 x 2 grid: B's column blocks from the root to their grid columns (the root's own column included)
+        D12 = DistributedOzakiCRT(grid=(1, world))
+        cols = n // world
+        parts = [B_full[:, q * cols:(q + 1) * cols].contiguous() for q in range(world)]
+        C, info = D12.run_broadcast_b(A_full, parts if rank == root else None, root=root)
+        out["cols"] = (C.cpu().numpy(), (info["N"], info["p"], info["preq"]))
         torch.cuda.synchronize()
         D.engine.check_errors()
         for name, (Cn, dec) in out.items():
@@ -97,7 +103,9 @@ def test_two_ranks_nccl_bit_exact(tmp_path):
         C = np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{r}.npy")) for r in range(world)])
         np.testing.assert_array_equal(C.view(np.uint64), single, err_msg=name)
     np.testing.assert_array_equal(np.load(os.path.join(tmp_path, f"root_{world - 1}.npy")).view(np.uint64), single)
-    for name in ("pre", "bcast", "root"):
+    C = np.concatenate([np.load(os.path.join(tmp_path, f"cols_{r}.npy")) for r in range(world)], axis=1)
+    np.testing.assert_array_equal(C.view(np.uint64), single, err_msg="cols")
+    for name in ("pre", "bcast", "root", "cols"):
         for r in range(world):
             assert eval(open(os.path.join(tmp_path, f"{name}_{r}.txt")).read()) == want, (name, r)
 
