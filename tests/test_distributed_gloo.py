@@ -105,7 +105,7 @@ class OracleOps:
         return C
 
 
-GRIDS = {"ok": (2, 1), "cols": (1, 2), "grid4": (2, 2), "cert": (2, 1), "cert4": (2, 2), "bcastB4": (2, 2)}
+GRIDS = {"ok": (2, 1), "cols": (1, 2), "grid4": (2, 2), "cert": (2, 1), "cert4": (2, 2), "bcastB4": (2, 2), "bcastB8": (4, 2)}
 
 
 def _worker(rank, world, port, outdir, mode):
@@ -133,15 +133,15 @@ def _worker(rank, world, port, outdir, mode):
         D = DistributedOzakiCRT(ops=OracleOps(O), grid=(R, S))
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure on rank 1 before the first collective")
-        if mode in ("bcastB", "bcastB4", "root"):
+        if mode in ("bcastB", "bcastB4", "bcastB8", "root"):
             # the operands start on rank 1 (the root): B only (A's rows on their owners), or A and B both
             root = 1
             Bfull = torch.from_numpy(B) if rank == root else None
-            if mode in ("bcastB", "bcastB4"):
+            if mode in ("bcastB", "bcastB4", "bcastB8"):
                 C, info = D.run_broadcast_b(Al, Bfull, root=root)
                 # on the grid the root may also hold B as its column blocks
                 Bparts = [torch.from_numpy(np.ascontiguousarray(B[:, q * cols:(q + 1) * cols])) for q in range(S)]
-                C2, info2 = D.run_broadcast_b(Al, Bparts if (mode == "bcastB4" and rank == root) else Bfull, root=root,
+                C2, info2 = D.run_broadcast_b(Al, Bparts if (mode != "bcastB" and rank == root) else Bfull, root=root,
                                               force_N=22)
             else:
                 Afull = torch.from_numpy(A) if rank == root else None
@@ -236,24 +236,26 @@ def test_broadcast_b_from_root_equals_single_process(oracle, tmp_path, pkg):
     assert infos[0] == infos[1] and infos[0][:3] == (iref["N"], iref["p"], iref["p_req"])
 
 
-def test_broadcast_b_on_grid_equals_single_process(oracle, tmp_path, pkg):
-    """B only on the root (rank 1) of a 2 x 2 grid: column block b of B goes to grid column b only (through one
-    communicator per column group, the root in both), the root computes all of B's column statistics; every rank
+@pytest.mark.parametrize("mode,world", [("bcastB4", 4), ("bcastB8", 8)])
+def test_broadcast_b_on_grid_equals_single_process(oracle, tmp_path, pkg, mode, world):
+    """B only on the root (rank 1) of a 2 x 2 or 4 x 2 grid: column block b of B goes to grid column b only (through
+    one communicator per column group, the root in both), the root computes all of B's column statistics; every rank
     multiplies A's row block a by B's column block b."""
-    alive = _spawn(4, "bcastB4", tmp_path)
+    R, S = GRIDS[mode]
+    alive = _spawn(world, mode, tmp_path)
     assert not any(alive)
     errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]
     assert not errs, open(os.path.join(tmp_path, errs[0])).read()
     A, B = pkg.make_inputs(128, 256, 128, 2.0, seed=31)
 
     def assemble(name):
-        return np.concatenate([np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{a * 2 + b}.npy"))
-                                               for b in range(2)], axis=1) for a in range(2)])
+        return np.concatenate([np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{a * S + b}.npy"))
+                                               for b in range(S)], axis=1) for a in range(R)])
     Cref, iref = oracle.run(A, B)
     np.testing.assert_array_equal(assemble("C").view(np.uint64), Cref.view(np.uint64))
     C22ref, i22 = oracle.run(A, B, force_N=22)
     np.testing.assert_array_equal(assemble("C22").view(np.uint64), C22ref.view(np.uint64))
-    infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(4)]
+    infos = [eval(open(os.path.join(tmp_path, f"info_{r}.txt")).read()) for r in range(world)]
     assert all(i == infos[0] for i in infos) and infos[0][:3] == (iref["N"], iref["p"], iref["p_req"])
 
 
