@@ -106,7 +106,15 @@ struct TcArgs {
     unsigned long long kdiv;          // A: floor(2^64 / k) + 1 (row of a flat index by one multiply-high)
     unsigned E;                       // A: m k
     int k, N, ntiles, lblocks;        // lblocks (B): tiles along the contraction index
+    unsigned long long ldiv;          // B: floor(2^64 / lblocks) + 1 for lblocks > 1 (column block by a multiply-high)
 };
+
+// B tile T -> (column block, contraction block): T / lblocks by a multiply-high, exact for T < 2^32 (lblocks = 1,
+// where floor(2^64 / lblocks) + 1 does not fit 64 bits, is the identity)
+__device__ __forceinline__ void b_tile(const TcArgs& a, int T, int& jb, int& lb) {
+    jb = a.lblocks == 1 ? T : (int)__umul64hi((unsigned long long)(unsigned)T, a.ldiv);
+    lb = T - jb * a.lblocks;
+}
 
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int32_t* err) {
     *abort_flag = 1;
@@ -259,7 +267,11 @@ __global__ void __launch_bounds__(stc::THREADS, 2)
         const int s = i % STAGES, T = (int)blockIdx.x + i * G;
         mbar_arrive_expect_tx(full_bar(s), (uint32_t)X_BYTES);
         const uint32_t dst = smem_addr(sX + s * X_BYTES);
-        if (IS_B) tma_load_2d(dst, &tmX, (T / a.lblocks) * 16, (T % a.lblocks) * 64, full_bar(s));
+        if (IS_B) {
+            int jb, lb;
+            b_tile(a, T, jb, lb);
+            tma_load_2d(dst, &tmX, jb * 16, lb * 64, full_bar(s));
+        }
         else tma_load_2d(dst, &tmX, 0, T * 64, full_bar(s));
         loads_issued++;
     };
@@ -293,7 +305,8 @@ __global__ void __launch_bounds__(stc::THREADS, 2)
 #pragma unroll
             for (int u = 0; u < 4; u++) ag[u] = base + __ldg(a.gam + l + u);
         } else {
-            const int jb = T / a.lblocks, lb = T - jb * a.lblocks;
+            int jb, lb;
+            b_tile(a, T, jb, lb);
             const int base = p - __ldg(a.vexp + jb * 16 + (R >> 3));
 #pragma unroll
             for (int u = 0; u < 4; u++) {
@@ -383,7 +396,8 @@ __global__ void __launch_bounds__(stc::THREADS, 2)
             off = (unsigned long long)T * TILE + 8ull * (unsigned)R;
             in = off < a.E;
         } else {
-            const int jb = T / a.lblocks, lb = T - jb * a.lblocks;
+            int jb, lb;
+            b_tile(a, T, jb, lb);
             const int l = lb * 64 + 8 * (R & 7);
             off = (unsigned long long)(jb * 16 + (R >> 3)) * (unsigned)a.k + (unsigned)l;
             in = l < a.k;
@@ -569,6 +583,7 @@ int ozk_split_tc_launch(int is_b, const double* src, const int32_t* vexp, const 
             return OZK_OK;
         args.E = (unsigned)E;
         args.lblocks = (k + 63) / 64;
+        args.ldiv = ~0ULL / (unsigned long long)args.lblocks + 1ULL;
         args.ntiles = (V / 16) * args.lblocks;
     }
     const int half = (N + 1) / 2;
