@@ -32,7 +32,8 @@
 //   string writes are free of bank conflicts (tau and tau + identity are both bijections).
 // * Pipeline per CTA (8 warps, two CTAs per SM for TMEM's 2 x 256 columns): TMA loads run STAGES tiles ahead; in
 //   iteration i all threads build tile i + 1's strings (second string buffer) while tile i's MMAs run, then read
-//   tile i's sums from TMEM and store its residues; after one CTA barrier thread 0 issues tile i + 1's MMAs.
+//   tile i's sums from TMEM and store its residues, then arrive (one arrival per warp) on an mbarrier; thread 0 alone
+//   waits for the eight arrivals and issues tile i + 1's MMAs and the next load, while the other warps go on.
 //   Every wait is bounded (4 s); a wait that runs out ORs OZK_DEVERR_TIMEOUT_SPLIT into *err and the CTA drains
 //   its loads and MMAs, frees TMEM and leaves.
 #include <cuda.h>
@@ -55,7 +56,7 @@ constexpr int STAGES = 5;
 constexpr int S_BYTES = ROWS * 128;          // one string tile
 constexpr int W_BYTES = 64 * 128;            // weight operand: up to 64 columns
 constexpr int TMEM_COLS = 256;
-constexpr int NUM_BARS = STAGES + 2;         // full[s], mma, drain
+constexpr int NUM_BARS = STAGES + 3;         // full[s], mma, drain, done
 // > 227 KB / 3: at most two CTAs per SM, as TMEM holds two allocations of 256 columns
 constexpr int SMEM_BYTES = 1024 + STAGES * X_BYTES + 2 * S_BYTES + W_BYTES + NUM_BARS * 8 + 16;
 constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;
@@ -225,12 +226,13 @@ __global__ void __launch_bounds__(stc::THREADS, 2)
     const int R = 32 * (warp & 3) + lane;                    // string row = TMEM lane
     const uint32_t bar0 = smem_addr(bars);
     auto full_bar = [&](int s) { return bar0 + 8u * (uint32_t)s; };
-    const uint32_t mma_bar = bar0 + 8u * STAGES, drain_bar = mma_bar + 8u;
+    const uint32_t mma_bar = bar0 + 8u * STAGES, drain_bar = mma_bar + 8u, done_bar = drain_bar + 8u;
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; s++) mbar_init(full_bar(s), 1);
         mbar_init(mma_bar, 1);
         mbar_init(drain_bar, 1);
+        mbar_init(done_bar, THREADS / 32);      // one arrival per warp and tile
         *abort_flag = 0;
         mbar_fence_init();
         tma_prefetch_desc(&tmX);
@@ -434,11 +436,25 @@ __global__ void __launch_bounds__(stc::THREADS, 2)
             if (i + 2 < nloc) fetch_ag(i + 2, ag_next);
         }
         ok = store_residues(i) && ok;
+        // this warp is done with tile i's TMEM and with tile i + 1's strings and input stage: one arrival; only the
+        // issuing thread waits for all warps, the others go on to the next tile
         tc_fence_before();
-        if (__syncthreads_or(ok ? 0 : 1)) break;
-        if (tid == 0 && i + 1 < nloc) {
-            if (i + 1 + STAGES < nloc) issue_load(i + 1 + STAGES);
-            issue_mma(i + 1);
+        ok = __all_sync(0xffffffffu, ok);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(done_bar);
+        if (!ok) break;
+        if (warp == 0 && i + 1 < nloc) {
+            bool got = true;
+            if (lane == 0) {
+                got = mbar_wait_bounded(done_bar, (uint32_t)(i & 1), abort_flag, WAIT_LIMIT_NS);
+                if (!got) {
+                    if (!*abort_flag) raise_abort(abort_flag, a.err);
+                } else {
+                    if (i + 1 + STAGES < nloc) issue_load(i + 1 + STAGES);
+                    issue_mma(i + 1);
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) break;   // warp 0 leaves as one
         }
     }
 
