@@ -1,8 +1,8 @@
 """Generate the golden vectors that pin the CPU oracle (oracle/) to the reference engine.
 
-Run in a container that has the reference checkout (read-only) at $OZAKI_REFERENCE (default /root/reference):
+Run where a checkout of the reference (read-only is enough) is at $OZAKI_REFERENCE:
 
-    python tests/golden/make_golden.py
+    OZAKI_REFERENCE=<path of the dl1683/matrix-numbers checkout> python tests/golden/make_golden.py
 
 It imports the reference's ``code/ozaki_engine.py`` on the CPU (no GPU needed; ENGINE_OUT is pointed at a temp
 dir) and records, from the reference's OWN functions:
@@ -33,10 +33,12 @@ import types
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("OZAKI_REFERENCE", "/root/reference")
+REF = os.environ.get("OZAKI_REFERENCE", "")
 
 
 def load_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "code")):
+        raise SystemExit("set OZAKI_REFERENCE to the path of a dl1683/matrix-numbers checkout")
     os.environ["ENGINE_OUT"] = tempfile.mkdtemp(prefix="ozaki_ref_out_")
     sys.path.insert(0, os.path.join(REF, "code"))
     import ozaki_engine as oe  # noqa: E402  (the reference, imported read-only)

@@ -9,7 +9,7 @@ as the reference's own ``cmd_check`` runs at its benchmark sizes (code/ozaki_eng
 * c3 (16384^3, phi 2): the same decision check, and 16 sampled rows (2048 columns each) bit for bit.
 * c5 (2048 x 262144 x 2048, alternating signs, N forced to 16): the decision at full size and a sampled block; and a
   reduced c5 (m = n = 64, k = 262144) whose whole ``run`` equals ``oracle.run``.  k > 131071 lies beyond the
-  reference's own limit (:1316), so the oracle's int64 products are the only judge there.
+  reference's own limit (:1316), so the oracle's int64 products are the only check there.
 
 Bar: N, p, p_req exact; C bit-exact (exact CRT + the reference's rounding).  Each large test builds its own engine and
 frees it, so the device never holds more than one configuration's planes."""
