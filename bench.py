@@ -232,7 +232,7 @@ def run_reference(args):
     if args.planes:
         forceN = args.planes
     oracle = _oracle()
-    threads = oracle.num_threads()
+    threads = oracle.set_threads(len(os.sched_getaffinity(0)))   # all host cores, also under torchrun
     A, B = pkg.make_inputs(m, k, n, phi, 0, alt)
     st, N, p = oracle_decision(oracle, A, B, forceN)
     s = args.cpu_sample or auto_sample(k, N, threads) // 2

@@ -70,6 +70,8 @@ def lib():
         L.ozo_core.argtypes = [P, P, P, P, P, i32, i32, i32, i32, i32, P]
         L.ozo_core.restype = i32
         L.ozo_num_threads.restype = i32
+        L.ozo_set_threads.argtypes = [i32]
+        L.ozo_set_threads.restype = None
         _lib = L
     return _lib
 
@@ -84,6 +86,12 @@ def _c64(a):
 
 def num_threads() -> int:
     return int(lib().ozo_num_threads())
+
+
+def set_threads(n: int) -> int:
+    """Run the parallel loops on n threads (overrides OMP_NUM_THREADS); returns the count now in effect."""
+    lib().ozo_set_threads(int(n))
+    return num_threads()
 
 
 def stats(A, B, inside=True):
