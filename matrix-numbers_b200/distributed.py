@@ -215,7 +215,9 @@ class DistributedOzakiCRT:
     """``run(A_block, B_block, C_block)``: this rank's block of C = A B, with the plane count and scalings of the
     whole product.  Rank g = a S + b passes rows [a m/R, (a+1) m/R) of A and columns [b n/S, (b+1) n/S) of B (as a
     contiguous k x n/S matrix); every rank must call ``run`` with the same block shapes and arguments.
-    ``grid=(R, S)`` (default ``default_grid(world)``)."""
+    ``grid=(R, S)`` (default ``default_grid(world)``).  The constructor and the first ``run_broadcast_b`` for a root
+    create extra communicators with ``torch.distributed.new_group``, which every process of the default group must
+    call: with a sub-group, construct the object (and make that first call) on every process, in the same order."""
 
     def __init__(self, group=None, ops=None, grid=None):
         self.group = group
