@@ -117,14 +117,14 @@ class CudaOps:
         """Column statistics (c, sB, nB) of all of B (k x n) with this rank's gamma (``st["gam"]``, from the global
         maxima): the root's share of ``run_broadcast_b``."""
         k, n = B.shape
-        out = self._glob.get(("cols", n))
+        out = self._glob.get(("cols", k, n))
         if out is None:
             out = {"c": torch.empty(n, dtype=torch.int32, device=B.device),
                    "sB": torch.empty(n, dtype=torch.float64, device=B.device),
                    "nB": torch.empty(n, dtype=torch.float64, device=B.device),
                    "ws": torch.empty(max(1, self.lib.ozk_stats_cols_workspace_bytes(k, n)), dtype=torch.uint8,
                                      device=B.device)}
-            self._glob[("cols", n)] = out
+            self._glob[("cols", k, n)] = out
         check(self.lib.ozk_stats_cols(ptr(B), k, n, ptr(st["gam"]), ptr(out["c"]), ptr(out["sB"]), ptr(out["nB"]),
                                       ptr(out["ws"]), out["ws"].numel(), self._stream()), "ozk_stats_cols")
         self.engine.launches += 2
