@@ -9,9 +9,10 @@ on inputs resident in HBM.  Default workload: the metric's n = 16384 configurati
 (U - 0.5) exp(2 N(0,1)), seed 0, dynamic plane rule).  With --gpus N > 1 the same product is split into an R x S
 grid of C blocks, one per rank (DistributedOzakiCRT: S = 2 from 4 ranks on, else row blocks; strong scaling).
 
-Printed (rank 0, one JSON line): value (device time, max over ranks), e2e (the same call from pinned host buffers,
-H2D + D2H inside the timed region), roofline of the INT8 product kernel (live CUDA-event time of its launches), the
-CPU baseline (the C/OpenMP port of the reference's algorithm on a bounded sample), clocks sampled by nvidia-smi during
+Printed (rank 0, one JSON line): value (device time, max over ranks), e2e (the same product from pinned host
+buffers, H2D + D2H inside the timed region: OzakiCRT.run_host_many on one GPU, DistributedOzakiCRT.run_host_many
+with each rank loading its share of the operands on N), roofline of the INT8 product kernel (live CUDA-event
+time of its launches), the CPU baseline (the C/OpenMP port of the reference's algorithm on a bounded sample), clocks sampled by nvidia-smi during
 the timed region, and the count of this library's kernel launches.
 
 ``--impl reference`` times the reference's algorithm on the host cores instead (the CPU port in oracle/, all
@@ -430,8 +431,6 @@ def main():
                     for q in range(S)] if (rank == 0 and S > 1) else B_root)
         C = torch.empty((rows, cols), dtype=torch.float64, device=dev)
         D = pkg.DistributedOzakiCRT(grid=(R, S))
-        # the ranks of each grid row share A's row block: the end-to-end step uploads half of it on each and gathers
-        row_groups = [dist.new_group([a * S + q for q in range(S)]) for a in range(R)] if S > 1 else None
         engine = D.engine
         call = lambda ev=None: D.run_broadcast_b(A, B_parts, C, root=0, force_N=forceN, certify=cert, events=ev)  # noqa: E731
         launches_of = lambda: D.launches  # noqa: E731
@@ -537,19 +536,11 @@ def main():
     # end to end through the public API with host buffers (pinned), H2D + D2H inside the timed region
     e2e = None
     if args.e2e_steps > 0:
-        ra, rb = divmod(rank, S)
-        sub_rows = rows // S                                   # this rank's share of the upload of A's row block
-        Ah = torch.from_numpy(np.ascontiguousarray(
-            A_host[ra * rows + rb * sub_rows:ra * rows + (rb + 1) * sub_rows])).pin_memory()
-        A_half = torch.empty((sub_rows, k), dtype=torch.float64, device=dev) if S > 1 else None
+        single = None
         if world == 1:
+            Ah = torch.from_numpy(A_host).pin_memory()
             Bh = torch.from_numpy(B_host).pin_memory()
-        elif rank == 0:
-            Bh = [torch.from_numpy(np.ascontiguousarray(B_host[:, q * cols:(q + 1) * cols])).pin_memory()
-                  for q in range(S)] if S > 1 else torch.from_numpy(B_host).pin_memory()
-        else:
-            Bh = None
-        Ch = torch.empty((rows, cols), dtype=torch.float64).pin_memory()
+            Ch = torch.empty((m, n), dtype=torch.float64).pin_memory()
         if world == 1 and args.mode == "sampled":
             E.run_host(Ah, Bh, Ch, force_N=forceN)             # warm-up of the host-buffer path
             torch.cuda.synchronize()
@@ -571,30 +562,37 @@ def main():
                    "D2H inside the timed region, the next step's H2D overlapped with this step's product)")
             single = {"value": flops / t_single / 1e12, "ms_per_step": t_single * 1e3,
                       "api": "OzakiCRT.run_host (one call at a time)"}
-        else:
-            # every step: H2D of this rank's A rows (and of B on rank 0), the headline call, D2H of the C rows
+        elif world == 1:
             def host_step(ev=None):
-                if S > 1:
-                    A_half.copy_(Ah, non_blocking=True)
-                    dist.all_gather_into_tensor(A, A_half, group=row_groups[ra])
-                else:
-                    A.copy_(Ah, non_blocking=True)
-                if world > 1 and rank == 0:
-                    if S > 1:
-                        for q in range(S):
-                            B_parts[q].copy_(Bh[q], non_blocking=True)
-                    else:
-                        B_root.copy_(Bh, non_blocking=True)
-                elif world == 1:
-                    B.copy_(Bh, non_blocking=True)
+                A.copy_(Ah, non_blocking=True)
+                B.copy_(Bh, non_blocking=True)
                 out = call(None)
                 Ch.copy_(C, non_blocking=True)
                 return out
             t_e2e, _, _, _ = timed_calls(torch, dist, host_step, args.e2e_steps, 1, world, stream)
-            api = ("per rank: H2D of its share of A's row block (the ranks of a grid row gather it over NCCL), rank 0 "
-                   "also H2D of B, DistributedOzakiCRT.run_broadcast_b, D2H of its block of C" if world > 1
-                   else "H2D of A and B, OzakiCRT.run_fast, D2H of C")
-            single = None
+            api = "H2D of A and B, OzakiCRT.run_fast, D2H of C"
+        else:
+            # every rank loads its share of its blocks from pinned host memory (each byte of A and B crosses PCIe
+            # once, spread over all ranks' links), the grid rows and columns gather the blocks over NCCL, then the
+            # grid product and the D2H of each C block; the next step's loads and this step's D2H overlap the product
+            eR, eS = default_grid(world)
+            ea, eb = divmod(rank, eS)
+            br, bc = m // eR, n // eS
+            sr, sk = br // eS, k // eR
+            Ah = torch.from_numpy(np.ascontiguousarray(A_host[ea * br + eb * sr:ea * br + (eb + 1) * sr])).pin_memory()
+            Bh = torch.from_numpy(np.ascontiguousarray(B_host[ea * sk:(ea + 1) * sk, eb * bc:(eb + 1) * bc])).pin_memory()
+            Ch = torch.empty((br, bc), dtype=torch.float64).pin_memory()
+            assert (eR, eS) == (D.R, D.S)
+            kw_e = dict(shares=True, force_N=forceN, certify=args.mode == "certified")
+            D.run_host_many([(Ah, Bh, Ch)] * 2, **kw_e)              # warm-up of both slots
+            t_e2e, _, _, _ = timed_calls(
+                torch, dist, lambda ev=None: D.run_host_many([(Ah, Bh, Ch)] * args.e2e_steps, **kw_e)[-1],
+                1, 0, world, stream)
+            t_e2e /= args.e2e_steps
+            api = (f"DistributedOzakiCRT.run_host_many(shares=True) on the {eR} x {eS} grid, {args.e2e_steps} products: "
+                   "each rank H2D of its share of A's row block and of B's column block, all_gather within grid rows "
+                   "and columns, the grid product, D2H of its C block; the next step's H2D and this step's D2H "
+                   "overlap the product")
         e2e = {"value": flops / t_e2e / 1e12, "unit": "TFLOPS", "ms_per_step": t_e2e * 1e3, "api": api,
                "h2d_bytes_per_step": (m * k + k * n) * 8, "d2h_bytes_per_step": m * n * 8}
         if single is not None:

@@ -36,6 +36,12 @@ B).  Two more entry points move the operands over NCCL inside the call:
   scattered, the statistics overlap the broadcast as above, and (with ``gather=True``) the row blocks of C are
   gathered back into the root's C.
 
+From host memory, ``run_host_many`` streams products whose operands start in pinned host buffers: with
+``shares=True`` each rank loads only its share of its blocks (1 / S of A's row block, 1 / R of B's column block, so
+that every byte of A and B crosses PCIe once, spread over all ranks' links), ``gather_shares`` assembles the blocks
+with one all_gather per grid row and column, and the next job's loads and the previous job's C block overlap the
+product.
+
 Every collective is NCCL's (no peer-memory loads, no TMA multicast): the exchanges are plain operand moves and small
 statistics vectors, with no computation to fuse them with.  ``events`` (a list) receives (name, CUDA event) marks
 after each phase, for per-stage timing on each rank.
@@ -215,9 +221,10 @@ class DistributedOzakiCRT:
     """``run(A_block, B_block, C_block)``: this rank's block of C = A B, with the plane count and scalings of the
     whole product.  Rank g = a S + b passes rows [a m/R, (a+1) m/R) of A and columns [b n/S, (b+1) n/S) of B (as a
     contiguous k x n/S matrix); every rank must call ``run`` with the same block shapes and arguments.
-    ``grid=(R, S)`` (default ``default_grid(world)``).  The constructor and the first ``run_broadcast_b`` for a root
-    create extra communicators with ``torch.distributed.new_group``, which every process of the default group must
-    call: with a sub-group, construct the object (and make that first call) on every process, in the same order."""
+    ``grid=(R, S)`` (default ``default_grid(world)``).  The constructor, the first ``run_broadcast_b`` for a root and
+    the first ``gather_shares`` (or ``run_host_many(shares=True)``) create extra communicators with
+    ``torch.distributed.new_group``, which every process of the default group must call: with a sub-group, construct
+    the object (and make those first calls) on every process, in the same order."""
 
     def __init__(self, group=None, ops=None, grid=None):
         self.group = group
@@ -421,6 +428,41 @@ class DistributedOzakiCRT:
         return self._decide_and_core(A, Bl, C, st, glob, m, n, k, row_begin, col_begin, tau, force_N, seed, force_p,
                                      safety, certify, events)
 
+    def _grid_groups(self):
+        """(communicator of this rank's grid row, of its grid column); None for a row or column of one rank.
+        Created on first use: every rank creates all of them in the same order (new_group is collective)."""
+        gg = self.__dict__.get("_gridgroups")
+        if gg is None:
+            base = dist.get_process_group_ranks(self.group) if self.group is not None else list(range(self.world))
+            rowg = [dist.new_group(ranks=[base[a * self.S + q] for q in range(self.S)]) if self.S > 1 else None
+                    for a in range(self.R)]
+            colg = [dist.new_group(ranks=[base[a * self.S + b] for a in range(self.R)]) if self.R > 1 else None
+                    for b in range(self.S)]
+            gg = self._gridgroups = (rowg[self.a], colg[self.b])
+        return gg
+
+    def gather_shares(self, A_share, B_share, A=None, B=None):
+        """This rank's blocks from the shares of its grid row and grid column.  Rank (a, b) holds rows
+        [b rows / S, (b + 1) rows / S) of A's row block a and rows [a k / R, (a + 1) k / R) of B's column block b
+        (k x n / S); one all_gather over the grid row gives the row block (rows x k), one over the grid column the
+        column block (k x n / S), so that every byte of A and B is loaded onto the GPUs once.  Every rank calls it
+        with shares of the same shapes.  Returns (A_block, B_block), written into A, B when given."""
+        rowg, colg = self._grid_groups()
+        rs, k = A_share.shape
+        ks, cols = B_share.shape
+        assert ks * self.R == k, "B's share must hold k / R rows of its column block"
+        if A is None:
+            A = A_share if rowg is None else torch.empty((rs * self.S, k), dtype=A_share.dtype, device=A_share.device)
+        if B is None:
+            B = B_share if colg is None else torch.empty((k, cols), dtype=B_share.dtype, device=B_share.device)
+        for full, share, g in ((A, A_share, rowg), (B, B_share, colg)):
+            if g is None:
+                if full.data_ptr() != share.data_ptr():
+                    full.copy_(share)
+            else:
+                dist.all_gather_into_tensor(full, share.contiguous(), group=g)
+        return A, B
+
     def run(self, A, B, C=None, tau=2.0 ** -52, force_N=None, inside=True, seed=0, force_p=None, safety=2.0,
             config=None, certify=False, events=None):
         if config is not None:
@@ -485,24 +527,37 @@ class DistributedOzakiCRT:
                    "cols": [col_begin, col_begin + cols], "grid": [self.R, self.S], "world": self.world}
 
 
-    def run_host_many(self, jobs, **kw):
+    def run_host_many(self, jobs, shares=False, **kw):
         """A stream of host-buffer products on this rank: ``jobs`` is a list of (A_rows_h, B_cols_h, C_block_h)
         pinned float64 CPU tensors of one shape (C_block_h None to allocate), the same list length and keyword
         arguments (those of ``run``) on every rank.  Two device slots: the H2D copies of job i + 1 run on their own
         stream while job i computes (its collectives included) and its C block goes back on a third stream.
+        ``shares=True``: A_rows_h and B_cols_h are this rank's shares as ``gather_shares`` defines them (rows / S of
+        A's row block, k / R rows of B's column block), so that each byte of A and B crosses PCIe once, on one rank;
+        the blocks are gathered over NCCL within the grid row and column before each product.
         Returns [(C_block_h, info), ...]; each equals a ``run`` on the same blocks bit for bit."""
         if not jobs:
             return []
         rows, k = jobs[0][0].shape
-        cols = jobs[0][1].shape[1]
+        ks, cols = jobs[0][1].shape
+        split_a = shares and self.S > 1
+        split_b = shares and self.R > 1
+        if shares:
+            rows, k = rows * self.S, ks * self.R
+            assert jobs[0][0].shape[1] == k, "A's share must hold all k columns"
         dev = torch.device("cuda", torch.cuda.current_device())
-        key = (rows, cols, k)
+        key = (rows, cols, k, split_a, split_b)
         io = self.__dict__.setdefault("_host_many", {})
         dv = io.get(key)
         if dv is None:
             io.clear()
-            dv = {"slots": [{x: torch.empty(sh, dtype=torch.float64, device=dev)
-                             for x, sh in (("A", (rows, k)), ("B", (k, cols)), ("C", (rows, cols)))} for _ in range(2)],
+            shapes = [("A", (rows, k)), ("B", (k, cols)), ("C", (rows, cols))]
+            if split_a:
+                shapes.append(("As", (rows // self.S, k)))
+            if split_b:
+                shapes.append(("Bs", (k // self.R, cols)))
+            dv = {"slots": [{x: torch.empty(sh, dtype=torch.float64, device=dev) for x, sh in shapes}
+                            for _ in range(2)],
                   "cin": torch.cuda.Stream(), "cout": torch.cuda.Stream()}
             io[key] = dv
         slots, cin, cout = dv["slots"], dv["cin"], dv["cout"]
@@ -519,8 +574,8 @@ class DistributedOzakiCRT:
             if used[s] is not None:
                 cin.wait_event(used[s][0])
             with torch.cuda.stream(cin):
-                slots[s]["A"].copy_(jobs[i][0], non_blocking=True)
-                slots[s]["B"].copy_(jobs[i][1], non_blocking=True)
+                slots[s]["As" if split_a else "A"].copy_(jobs[i][0], non_blocking=True)
+                slots[s]["Bs" if split_b else "B"].copy_(jobs[i][1], non_blocking=True)
             in_done[s].record(cin)
 
         h2d(0)
@@ -532,6 +587,11 @@ class DistributedOzakiCRT:
             cur.wait_event(in_done[s])
             if used[s] is not None:
                 cur.wait_event(used[s][1])
+            if shares:
+                # the gathers run on the current stream's order, before the product (the next H2D into this slot's
+                # shares waits for the event recorded after the product)
+                self.gather_shares(slots[s]["As"] if split_a else slots[s]["A"],
+                                   slots[s]["Bs"] if split_b else slots[s]["B"], slots[s]["A"], slots[s]["B"])
             C, info = self.run(slots[s]["A"], slots[s]["B"], slots[s]["C"], **kw)
             cdone, odone = torch.cuda.Event(), torch.cuda.Event()
             cdone.record(cur)

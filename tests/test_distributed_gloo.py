@@ -105,7 +105,8 @@ class OracleOps:
         return C
 
 
-GRIDS = {"ok": (2, 1), "cols": (1, 2), "grid4": (2, 2), "cert": (2, 1), "cert4": (2, 2), "bcastB4": (2, 2), "bcastB8": (4, 2)}
+GRIDS = {"ok": (2, 1), "cols": (1, 2), "grid4": (2, 2), "cert": (2, 1), "cert4": (2, 2), "bcastB4": (2, 2), "bcastB8": (4, 2),
+         "sharesR": (2, 1), "sharesS": (1, 2), "shares8": (4, 2)}
 
 
 def _worker(rank, world, port, outdir, mode):
@@ -151,6 +152,18 @@ def _worker(rank, world, port, outdir, mode):
                     C, C2 = torch.zeros(m, n, dtype=torch.float64), torch.zeros(m, n, dtype=torch.float64)
                 Cb, _ = D.run_from_root(Afull, Bfull, root=root, gather=False)
                 np.save(os.path.join(outdir, f"Cblock_{rank}.npy"), Cb.numpy())
+        elif mode.startswith("shares"):
+            # each rank holds 1 / S of A's row block and 1 / R of B's column block; the grid row and column gather
+            sr, sk = rows // S, k // R
+            As = torch.from_numpy(np.ascontiguousarray(A[a * rows + b * sr:a * rows + (b + 1) * sr]))
+            Bs = torch.from_numpy(np.ascontiguousarray(B[a * sk:(a + 1) * sk, b * cols:(b + 1) * cols]))
+            Ab, Bb = D.gather_shares(As, Bs)
+            assert torch.equal(Ab, Al) and torch.equal(Bb, Bt), "gathered blocks differ from the blocks"
+            Ab2, Bb2 = torch.empty_like(Al), torch.empty_like(Bt)
+            D.gather_shares(As, Bs, Ab2, Bb2)
+            assert torch.equal(Ab2, Al) and torch.equal(Bb2, Bt), "gather into given buffers"
+            C, info = D.run(Ab, Bb)
+            C2, info2 = D.run(Ab2, Bb2, force_N=22)
         else:
             C, info = D.run(Al, Bt, certify=mode.startswith("cert"))
             C2, info2 = D.run(Al, Bt, force_N=22)
@@ -177,8 +190,11 @@ def _spawn(world, mode, tmp_path):
     return alive
 
 
-@pytest.mark.parametrize("mode,world", [("ok", 2), ("cols", 2), ("grid4", 4)])
+@pytest.mark.parametrize("mode,world", [("ok", 2), ("cols", 2), ("grid4", 4), ("sharesR", 2), ("sharesS", 2),
+                                        ("shares8", 8)])
 def test_blocks_equal_single_process(oracle, tmp_path, pkg, mode, world):
+    """Pre-placed blocks (ok, cols, grid4), or blocks assembled by gather_shares from each rank's share of them
+    (shares*: the host-buffer path's loads), then the grid product."""
     alive = _spawn(world, mode, tmp_path)
     assert not any(alive)
     errs = [f for f in os.listdir(tmp_path) if f.startswith("error_")]

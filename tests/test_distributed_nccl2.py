@@ -1,6 +1,7 @@
 """DistributedOzakiCRT over NCCL on two GPUs (skipped when the machine has fewer): the pre-placed grid of C blocks, B
-broadcast from one rank inside the call, and A, B on one rank with scatter / broadcast / gather; and on four GPUs (a
-2 x 2 grid) B's column blocks sent from one rank to their grid columns.  Every C must equal the single-GPU product bit
+broadcast from one rank inside the call, A, B on one rank with scatter / broadcast / gather, and host buffers of which
+each rank loads only its share (run_host_many(shares=True)); and on four GPUs (a 2 x 2 grid) B's column blocks sent
+from one rank to their grid columns, and the host-share path.  Every C must equal the single-GPU product bit
 for bit, and every rank must decide the same (N, p).  The ranks are spawned child processes, one per GPU; the process
 group has a short timeout so that a failure ends the test instead of hanging it."""
 import os
@@ -21,6 +22,28 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _host_shares(pkg, D, A, B, rank):
+    """DistributedOzakiCRT.run_host_many(shares=True) over three jobs (B, -B, B): rank (a, b) passes rows / S rows
+    of A's row block a and k / R rows of B's column block b from pinned host memory.  The second product must be the
+    negation of the first (the symmetric lift and the rounding are odd), the third equal to the first."""
+    import torch
+    R, S = D.R, D.S
+    a, b = divmod(rank, S)
+    m, k = A.shape
+    n = B.shape[1]
+    br, bc = m // R, n // S
+    sr, sk = br // S, k // R
+    Ah = torch.from_numpy(np.ascontiguousarray(A[a * br + b * sr:a * br + (b + 1) * sr])).pin_memory()
+    Bh = torch.from_numpy(np.ascontiguousarray(B[a * sk:(a + 1) * sk, b * bc:(b + 1) * bc])).pin_memory()
+    Bn = torch.from_numpy(np.ascontiguousarray(-B[a * sk:(a + 1) * sk, b * bc:(b + 1) * bc])).pin_memory()
+    res = D.run_host_many([(Ah, Bh, None), (Ah, Bn, None), (Ah, Bh, None)], shares=True)
+    C0, C1, C2 = (x[0].numpy() for x in res)
+    assert np.array_equal(C1.view(np.uint64), (-C0).view(np.uint64)), "second job (negated B)"
+    assert np.array_equal(C2.view(np.uint64), C0.view(np.uint64)), "third job (slot reuse)"
+    info = res[0][1]
+    return C0.copy(), (info["N"], info["p"], info["preq"])
 
 
 def _worker(rank, world, port, outdir):
@@ -61,6 +84,9 @@ def _worker(rank, world, port, outdir):
         parts = [B_full[:, q * cols:(q + 1) * cols].contiguous() for q in range(world)]
         C, info = D12.run_broadcast_b(A_full, parts if rank == root else None, root=root)
         out["cols"] = (C.cpu().numpy(), (info["N"], info["p"], info["preq"]))
+        # host buffers, each rank loading only its share of its blocks, on both grids
+        for name, Dx in (("hostR", D), ("hostS", D12)):
+            out[name] = _host_shares(pkg, Dx, A, B, rank)
         torch.cuda.synchronize()
         D.engine.check_errors()
         for name, (Cn, dec) in out.items():
@@ -99,13 +125,14 @@ def test_two_ranks_nccl_bit_exact(tmp_path):
     assert not errs, open(os.path.join(tmp_path, errs[0])).read()
     single = np.load(os.path.join(tmp_path, "single.npy")).view(np.uint64)
     want = eval(open(os.path.join(tmp_path, "single.txt")).read())
-    for name in ("pre", "bcast"):
+    for name in ("pre", "bcast", "hostR"):
         C = np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{r}.npy")) for r in range(world)])
         np.testing.assert_array_equal(C.view(np.uint64), single, err_msg=name)
     np.testing.assert_array_equal(np.load(os.path.join(tmp_path, f"root_{world - 1}.npy")).view(np.uint64), single)
-    C = np.concatenate([np.load(os.path.join(tmp_path, f"cols_{r}.npy")) for r in range(world)], axis=1)
-    np.testing.assert_array_equal(C.view(np.uint64), single, err_msg="cols")
-    for name in ("pre", "bcast", "root", "cols"):
+    for name in ("cols", "hostS"):
+        C = np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{r}.npy")) for r in range(world)], axis=1)
+        np.testing.assert_array_equal(C.view(np.uint64), single, err_msg=name)
+    for name in ("pre", "bcast", "root", "cols", "hostR", "hostS"):
         for r in range(world):
             assert eval(open(os.path.join(tmp_path, f"{name}_{r}.txt")).read()) == want, (name, r)
 
@@ -138,12 +165,14 @@ def _worker_grid(rank, world, port, outdir):
         D = DistributedOzakiCRT(grid=(R, S))
         C, info = D.run_broadcast_b(A_rows, parts if rank == 0 else None, root=0)
         C2, info2 = D.run_broadcast_b(A_rows, torch.from_numpy(B).to(dev) if rank == 0 else None, root=0)
+        C3, dec3 = _host_shares(pkg, D, A, B, rank)
         torch.cuda.synchronize()
         D.engine.check_errors()
         np.save(os.path.join(outdir, f"grid_{rank}.npy"), C.cpu().numpy())
         np.save(os.path.join(outdir, f"grid2_{rank}.npy"), C2.cpu().numpy())
+        np.save(os.path.join(outdir, f"grid3_{rank}.npy"), C3)
         with open(os.path.join(outdir, f"grid_{rank}.txt"), "w") as f:
-            f.write(repr(((info["N"], info["p"], info["preq"]), (info2["N"], info2["p"], info2["preq"]))))
+            f.write(repr(((info["N"], info["p"], info["preq"]), (info2["N"], info2["p"], info2["preq"]), dec3)))
         if rank == 0:
             E = pkg.OzakiCRT()
             Cs, i_s = E.run(torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev))
@@ -176,10 +205,10 @@ def test_four_ranks_grid_broadcast_bit_exact(tmp_path):
     assert not errs, open(os.path.join(tmp_path, errs[0])).read()
     single = np.load(os.path.join(tmp_path, "single.npy")).view(np.uint64)
     want = eval(open(os.path.join(tmp_path, "single.txt")).read())
-    for name in ("grid", "grid2"):
+    for name in ("grid", "grid2", "grid3"):
         C = np.concatenate([np.concatenate([np.load(os.path.join(tmp_path, f"{name}_{a * 2 + b}.npy"))
                                             for b in range(2)], axis=1) for a in range(2)])
         np.testing.assert_array_equal(C.view(np.uint64), single, err_msg=name)
     for r in range(world):
         got = eval(open(os.path.join(tmp_path, f"grid_{r}.txt")).read())
-        assert got[0] == want and got[1] == want, (r, got, want)
+        assert got[0] == want and got[1] == want and got[2] == want, (r, got, want)
