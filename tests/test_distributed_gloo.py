@@ -159,6 +159,11 @@ def _worker(rank, world, port, outdir, mode):
             Bs = torch.from_numpy(np.ascontiguousarray(B[a * sk:(a + 1) * sk, b * cols:(b + 1) * cols]))
             Ab, Bb = D.gather_shares(As, Bs)
             assert torch.equal(Ab, Al) and torch.equal(Bb, Bt), "gathered blocks differ from the blocks"
+            try:                                    # a share of the wrong height fails before any collective
+                D.gather_shares(As, Bs[:-1])
+                raise RuntimeError("a B share of k / R - 1 rows was accepted")
+            except AssertionError:
+                pass
             Ab2, Bb2 = torch.empty_like(Al), torch.empty_like(Bt)
             D.gather_shares(As, Bs, Ab2, Bb2)
             assert torch.equal(Ab2, Al) and torch.equal(Bb2, Bt), "gather into given buffers"
