@@ -535,7 +535,8 @@ class DistributedOzakiCRT:
         ``shares=True``: A_rows_h and B_cols_h are this rank's shares as ``gather_shares`` defines them (rows / S of
         A's row block, k / R rows of B's column block), so that each byte of A and B crosses PCIe once, on one rank;
         the blocks are gathered over NCCL within the grid row and column before each product.
-        Returns [(C_block_h, info), ...]; each equals a ``run`` on the same blocks bit for bit."""
+        Returns [(C_block_h, info), ...]; each equals a ``run`` on the same blocks bit for bit.  Synchronises at the
+        end and raises ``OzkError`` if a kernel of these products reported a device-side error."""
         if not jobs:
             return []
         rows, k = jobs[0][0].shape
@@ -604,6 +605,7 @@ class DistributedOzakiCRT:
         cur.wait_stream(cout)
         cur.wait_stream(cin)
         cur.synchronize()
+        self.engine.check_errors()           # raises if a split, product or reconstruction reported a device error
         return results
 
 
