@@ -455,6 +455,7 @@ class DistributedOzakiCRT:
             A = A_share if rowg is None else torch.empty((rs * self.S, k), dtype=A_share.dtype, device=A_share.device)
         if B is None:
             B = B_share if colg is None else torch.empty((k, cols), dtype=B_share.dtype, device=B_share.device)
+        assert tuple(A.shape) == (rs * self.S, k) and tuple(B.shape) == (k, cols), "block buffers of the wrong shape"
         for full, share, g in ((A, A_share, rowg), (B, B_share, colg)):
             if g is None:
                 if full.data_ptr() != share.data_ptr():

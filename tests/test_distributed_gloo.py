@@ -164,6 +164,11 @@ def _worker(rank, world, port, outdir, mode):
                 raise RuntimeError("a B share of k / R - 1 rows was accepted")
             except AssertionError:
                 pass
+            try:                                    # so does a block buffer of the wrong shape
+                D.gather_shares(As, Bs, torch.empty(rows + 4, k, dtype=torch.float64), None)
+                raise RuntimeError("an A block buffer of rows + 4 rows was accepted")
+            except AssertionError:
+                pass
             Ab2, Bb2 = torch.empty_like(Al), torch.empty_like(Bt)
             D.gather_shares(As, Bs, Ab2, Bb2)
             assert torch.equal(Ab2, Al) and torch.equal(Bb2, Bt), "gather into given buffers"
