@@ -12,8 +12,8 @@ grid of C blocks, one per rank (DistributedOzakiCRT: S = 2 from 4 ranks on, else
 Printed (rank 0, one JSON line): value (device time, max over ranks), e2e (the same product from pinned host
 buffers, H2D + D2H inside the timed region: OzakiCRT.run_host_many on one GPU, DistributedOzakiCRT.run_host_many
 with each rank loading its share of the operands on N), roofline of the INT8 product kernel (live CUDA-event
-time of its launches), the CPU baseline (the C/OpenMP port of the reference's algorithm on a bounded sample), clocks sampled by nvidia-smi during
-the timed region, and the count of this library's kernel launches.
+time of its launches), the CPU baseline (the C/OpenMP port of the reference's algorithm on a bounded sample),
+clocks sampled by nvidia-smi during the timed region, and the count of this library's kernel launches.
 
 ``--impl reference`` times the reference's algorithm on the host cores instead (the CPU port in oracle/, all
 threads), on a bounded sample of the same workload, and prints the same line with "impl": "reference".
@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="c3")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=6)
+    ap.add_argument("--e2e-steps", type=int, default=-1,
+                    help="products in the end-to-end stream from host buffers (default: max(6, --steps); 0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-accuracy", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=0, help="rows = cols of the CPU sample block (0: auto)")
@@ -61,7 +62,10 @@ def parse():
     ap.add_argument("--q", type=int, default=4, help="products per step in --mode persist")
     ap.add_argument("--planes", type=int, default=0, help="force the plane count N (0: the workload's rule)")
     ap.add_argument("--clock-log", default="", help="also write the raw nvidia-smi clock samples to this CSV file")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.e2e_steps < 0:
+        args.e2e_steps = max(6, args.steps)
+    return args
 
 
 def workload_config(args, m, n, k, phi, planes, p, world, grid, products=1):
@@ -580,7 +584,8 @@ def main():
             br, bc = m // eR, n // eS
             sr, sk = br // eS, k // eR
             Ah = torch.from_numpy(np.ascontiguousarray(A_host[ea * br + eb * sr:ea * br + (eb + 1) * sr])).pin_memory()
-            Bh = torch.from_numpy(np.ascontiguousarray(B_host[ea * sk:(ea + 1) * sk, eb * bc:(eb + 1) * bc])).pin_memory()
+            Bh = torch.from_numpy(np.ascontiguousarray(B_host[ea * sk:(ea + 1) * sk, eb * bc:(eb + 1) * bc]))
+            Bh = Bh.pin_memory()
             Ch = torch.empty((br, bc), dtype=torch.float64).pin_memory()
             assert (eR, eS) == (D.R, D.S)
             kw_e = dict(shares=True, force_N=forceN, certify=args.mode == "certified")
@@ -589,8 +594,8 @@ def main():
                 torch, dist, lambda ev=None: D.run_host_many([(Ah, Bh, Ch)] * args.e2e_steps, **kw_e)[-1],
                 1, 0, world, stream)
             t_e2e /= args.e2e_steps
-            api = (f"DistributedOzakiCRT.run_host_many(shares=True) on the {eR} x {eS} grid, {args.e2e_steps} products: "
-                   "each rank H2D of its share of A's row block and of B's column block, all_gather within grid rows "
+            api = (f"DistributedOzakiCRT.run_host_many(shares=True) on the {eR} x {eS} grid, {args.e2e_steps} "
+                   "products: each rank H2D of its share of A's row block and of B's column block, all_gather within grid rows "
                    "and columns, the grid product, D2H of its C block; the next step's H2D and this step's D2H "
                    "overlap the product")
         e2e = {"value": flops / t_e2e / 1e12, "unit": "TFLOPS", "ms_per_step": t_e2e * 1e3, "api": api,
